@@ -1,0 +1,487 @@
+"""Benchmark of the B200 INT8 convrot linear (one JSON line on rank 0).
+
+Step (every N): the config-2 linear set of one attention block on this rank's tokens -- q, k, v and out convrot
+linears, K = N = 5120, rank-32 low-rank correction and bias, q/k/v sharing one quantisation -- with, for N > 1, the
+Ulysses seq<->head all-to-all of q, k, v ([M/P, 40 heads, 128] bf16) around an identity attention (o = v) and back.
+M = 32768 token rows per rank (weak scaling; N = 4 is BASELINE config 4's 131072 tokens).
+
+  value       INT8 TOPS of the whole job (4 GEMMs x 2*M*K*N per rank, all ranks) over the device-timed steps
+  e2e         the same metric through the public module API with host buffers: each step copies x from pinned
+              host memory and reads the out projection back to pinned host memory inside the timed region
+  roofline    the tcgen05 GEMM (dominant kernel): 2*M*N*K INT8 ops per launch over its CUDA-event duration in the
+              timed region, against the INT8 peak measured here (torch._int_mm = cuBLASLt, 8192^3)
+  extras      (N = 1) config 2's single linear (TOPS), config 3's DiT-block linear set (ms), rotate+quantise GB/s
+  cpu_baseline the reference's CPU path (_forward_torch, int8.py:173-179) as ported in oracle/ (numpy/BLAS),
+              on a bounded row sample, rank 0 at N = 1
+
+``--impl reference`` times that CPU port alone on the same metric (rank 0; other ranks exit at once).
+Inputs are seeded synthetic tensors (hyperflow_h3_flash_b200.synthetic); the per-step activations (335 MB) are larger
+than L2 (126 MB), so no L2 flush is needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_DIM = N_DIM = 5120
+RANK = 32
+HEADS, HEAD_DIM = 40, 128
+GROUP = 256
+SPEC_INT8_TOPS = 4500.0
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rows", type=int, default=32768, help="token rows per rank")
+    ap.add_argument("--no-extras", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms during the timed region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        loaded = [v for v in sm if mx and v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------------------- CPU arm
+
+
+def cpu_port_linear_set(rows: int, steps: int, warmup: int) -> dict:
+    """The reference's CPU path for the linear set, ported to numpy/BLAS, on `rows` token rows."""
+    import numpy as np
+    import torch
+
+    from hyperflow_h3_flash_b200 import synthetic
+    from oracle import oracle as O
+
+    cores = len(os.sched_getaffinity(0))
+    x = synthetic.activations(rows, K_DIM).view(torch.int16).numpy().view(np.uint16)
+    layers = [synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=i)
+              for i in range(4)]
+    h = O.regular_hadamard(GROUP)
+
+    def linear(xb, w):
+        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        y = O.bf16_to_f32(O.forward_cpu_port(xb, w.qweight.numpy(), w.wscale.numpy(), GROUP, h))
+        y = O.bf16_to_f32(O.f32_to_bf16(y + O.bf16_to_f32(bits(w.bias))[None, :]))
+        xa = O.f32_to_bf16(O.bf16_to_f32(xb) @ O.bf16_to_f32(bits(w.down)).T)
+        lr = O.f32_to_bf16(O.bf16_to_f32(xa) @ O.bf16_to_f32(bits(w.up)).T)
+        return O.f32_to_bf16(y + O.bf16_to_f32(lr))
+
+    def step():
+        q, k, v = (linear(x, layers[i]) for i in range(3))
+        return linear(v, layers[3])
+
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    ops = 4 * 2.0 * rows * K_DIM * N_DIM
+    t = statistics.median(times)
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"{rows} token rows of the linear set (4 linears {K_DIM}x{N_DIM}, r={RANK}, bias), "
+                      f"median of {steps} after {warmup} warm-up, numpy/BLAS port of _forward_torch "
+                      f"(int8.py:173-179) + bias + up(down(x))",
+            "seconds_per_step": t, "mean_seconds_per_step": statistics.mean(times)}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    rows = 1024
+    res = cpu_port_linear_set(rows, args.steps, args.warmup)
+    line = {
+        "metric": "INT8 convrot linear-set TOPS (q,k,v,out; K=N=5120, r=32)", "value": res["value"],
+        "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": "config-2 linear set, CPU sample", "rows_sampled": rows, "K": K_DIM, "N": N_DIM,
+                   "rank": RANK, "group": GROUP},
+        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": res["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------------- GPU arm
+
+
+def measure_int8_peak(torch, dev) -> dict:
+    """cuBLASLt INT8 (torch._int_mm) at 8192^3: best of 10 (burst) and a ~1.5 s loop (sustained)."""
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b.t())
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch._int_mm(a, b.t())
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, int(1500 / max(best, 1e-3)))
+    s.record()
+    for _ in range(reps):
+        torch._int_mm(a, b.t())
+    e.record()
+    e.synchronize()
+    ops = 2.0 * n**3
+    return {"burst_tops": ops / best / 1e9, "sustained_tops": ops * reps / s.elapsed_time(e) / 1e9}
+
+
+class KernelTimer:
+    """Counts this library's kernel launches and brackets GEMM / rotate launches with CUDA events on the launching
+    stream, by wrapping the module's kernel namespace."""
+
+    def __init__(self, torch, kernels):
+        self.torch = torch
+        self.kernels = kernels
+        self.saved = {}
+        self.launches = 0
+        self.active = False
+        self.gemm_events, self.rq_events = [], []
+        self.gemm_shapes, self.rq_shapes = [], []
+
+    def _wrap(self, name, kind, n_launch):
+        fn = getattr(self.kernels, name)
+        self.saved[name] = fn
+        torch = self.torch
+
+        def wrapped(*a, **k):
+            if not self.active:
+                return fn(*a, **k)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            out = fn(*a, **k)
+            e.record()
+            self.launches += n_launch
+            if kind == "gemm":
+                self.gemm_events.append((s, e))
+                self.gemm_shapes.append((a[0].shape[0], a[1].shape[0], a[0].shape[1]))
+            elif kind == "rq":
+                self.rq_events.append((s, e))
+                self.rq_shapes.append(tuple(a[0].shape))
+            return out
+
+        setattr(self.kernels, name, wrapped)
+
+    def __enter__(self):
+        self._wrap("convrot_matmul", "gemm", 1)
+        self._wrap("rotate_quant", "rq", 1)
+        self._wrap("rotate_quant_torch_rounding", "rq", 1)
+        self._wrap("lowrank_down", "down", 1)
+        return self
+
+    def __exit__(self, *exc):
+        for k, v in self.saved.items():
+            setattr(self.kernels, k, v)
+        return False
+
+    def reset(self):
+        self.launches = 0
+        self.gemm_events, self.rq_events, self.gemm_shapes, self.rq_shapes = [], [], [], []
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from hyperflow_h3_flash_b200 import int8 as I
+    from hyperflow_h3_flash_b200 import synthetic, ulysses
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    M = args.rows
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # ---- the linear set of one attention block
+    def make_layer(i, K, N, rank_lr, bias=True):
+        w = synthetic.linear_weights(K, N, rank=rank_lr, bias=bias, group=GROUP, seed_offset=i)
+        layer = I.Int8RotLinear(K, N, GROUP, bias=bias, rank=rank_lr)
+        synthetic.load_into(layer, w)
+        return layer.to(dev)
+
+    to_q, to_k, to_v, to_out = (make_layer(i, K_DIM, N_DIM, RANK) for i in range(4))
+    to_q.keep_input = to_k.keep_input = True
+    x_host = synthetic.activations(M, K_DIM, seed=rank).pin_memory()
+    x = x_host.to(dev)
+    y_host = torch.empty(M, N_DIM, dtype=torch.bfloat16).pin_memory()
+
+    def step(inp):
+        return ulysses.attention_block_linears(inp, to_q, to_k, to_v, to_out, HEADS)
+
+    kernels = I._kernels()
+    timer = KernelTimer(torch, kernels)
+    with torch.inference_mode(), timer:
+        # device-timed steps, inputs resident in HBM
+        for _ in range(args.warmup):
+            step(x)
+        torch.cuda.synchronize()
+        barrier()
+        timer.active = True
+        timer.reset()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            torch.cuda.synchronize()
+            barrier()
+            start.record()
+            for _ in range(args.steps):
+                out = step(x)
+            end.record()
+            torch.cuda.synchronize()
+            barrier()
+        timer.active = False
+        ms = start.elapsed_time(end)
+        gemm_ms = [s.elapsed_time(e) for s, e in timer.gemm_events]
+        rq_ms = [s.elapsed_time(e) for s, e in timer.rq_events]
+        launches = timer.launches
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+
+        # e2e through the module API with host buffers (pinned H2D of x, D2H of the out projection)
+        for _ in range(max(1, args.warmup // 2)):
+            xd = x_host.to(dev, non_blocking=True)
+            y_host.copy_(step(xd), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        for _ in range(args.steps):
+            xd = x_host.to(dev, non_blocking=True)
+            y_host.copy_(step(xd), non_blocking=True)
+        e_end.record()
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e_start.elapsed_time(e_end)], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item())
+
+    ops_step = 4 * 2.0 * M * K_DIM * N_DIM
+    value = world * ops_step * args.steps / (ms_max * 1e-3) / 1e12
+    e2e_value = world * ops_step * args.steps / (e2e_ms * 1e-3) / 1e12
+
+    extras = {}
+    peak = None
+    if world == 1 and not args.no_extras:
+        with torch.inference_mode():
+            peak = measure_int8_peak(torch, dev)
+            extras = run_extras(torch, I, synthetic, dev, args, x)
+    gemm_avg = statistics.mean(gemm_ms) if gemm_ms else None
+    gemm_ops = 2.0 * M * K_DIM * N_DIM
+    achieved = gemm_ops / (gemm_avg * 1e-3) / 1e12 if gemm_avg else None
+    peak_tops = peak["sustained_tops"] if peak else None
+    roofline = {
+        "kernel": "convrot_gemm_kernel (tcgen05 kind::i8, 128x256 tiles, fused dequant+bias+low-rank epilogue)",
+        "bound": "tensor", "unit": "TFLOP/s", "achieved": achieved, "peak": peak_tops,
+        "frac": (achieved / peak_tops) if (achieved and peak_tops) else None,
+        "peak_source": "measured here: torch._int_mm (cuBLASLt INT8) 8192^3, sustained ~1.5 s loop"
+        if peak else None,
+        "frac_of_spec_4500": achieved / SPEC_INT8_TOPS if achieved else None,
+        "per_launch_ops": gemm_ops, "avg_launch_ms": gemm_avg, "launches_timed": len(gemm_ms),
+        "traffic": load_traffic("gemm"),
+    }
+    if peak:
+        roofline["int8_peak_burst_tops"] = peak["burst_tops"]
+    rq_avg = statistics.mean(rq_ms) if rq_ms else None
+    rq_bytes = M * K_DIM * 3 + 4 * M
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_extras:
+            cpu = cpu_port_linear_set(2048, 3, 1)
+            cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        line = {
+            "metric": "INT8 convrot linear-set TOPS (q,k,v,out; K=N=5120, r=32)",
+            "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, random-init weights)",
+            "config": {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
+                                   f"M={M} rows/rank, K=N={K_DIM}, r={RANK}, bias, group {GROUP}"
+                                   + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity "
+                                      "attention" if world > 1 else ""),
+                       "rows_per_rank": M, "total_rows": M * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
+                       "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (x is 335 MB per step), no flush"},
+            "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
+                    "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "rotate_quant": {"bound": "hbm", "avg_launch_ms": rq_avg, "bytes_per_launch": rq_bytes,
+                             "achieved_gbs": rq_bytes / (rq_avg * 1e-3) / 1e9 if rq_avg else None,
+                             "peak_gbs": measured_peak("hbm_gbs"),
+                             "traffic": load_traffic("rotate_quant")},
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        if line["rotate_quant"]["achieved_gbs"] and line["rotate_quant"]["peak_gbs"]:
+            line["rotate_quant"]["frac"] = line["rotate_quant"]["achieved_gbs"] / line["rotate_quant"]["peak_gbs"]
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_extras(torch, I, synthetic, dev, args, x) -> dict:
+    """Config 2's single linear, config 3's block set, rotate+quantise bandwidth (N = 1 only)."""
+    out = {}
+
+    def timed(fn, steps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) / steps
+
+    M = args.rows
+    w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=7)
+    layer = I.Int8RotLinear(K_DIM, N_DIM, GROUP, bias=True, rank=RANK)
+    synthetic.load_into(layer, w)
+    layer = layer.to(dev)
+    ms = timed(lambda: layer(x), args.steps)
+    out["single_linear"] = {"config": f"config 2: M={M}, K=N={K_DIM}, r={RANK}, bias", "ms": ms,
+                            "tops": 2.0 * M * K_DIM * N_DIM / (ms * 1e-3) / 1e12}
+    ms = timed(lambda: I.rotate_quant(x, GROUP), args.steps)
+    nbytes = M * K_DIM * 3 + 4 * M
+    out["rotate_quant_cfg2"] = {"ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "bytes": nbytes}
+    # config 3: DiT-block linear set at M = 32760, rank 64
+    Mb = 32760
+    xb = synthetic.activations(Mb, K_DIM, seed=1).to(dev)
+    hb = synthetic.activations(Mb, 13824, seed=2).to(dev)
+    shapes = [("qkv", K_DIM, 15360), ("out", K_DIM, K_DIM), ("ffn_up", K_DIM, 2 * 13824), ("ffn_down", 13824, K_DIM)]
+    layers = {}
+    for i, (name, K, N) in enumerate(shapes):
+        wl = synthetic.linear_weights(K, N, rank=64, bias=True, group=GROUP, seed_offset=20 + i)
+        ly = I.Int8RotLinear(K, N, GROUP, bias=True, rank=64)
+        synthetic.load_into(ly, wl)
+        layers[name] = ly.to(dev)
+        del wl
+
+    def block():
+        layers["qkv"](xb)
+        layers["out"](xb)
+        layers["ffn_up"](xb)
+        layers["ffn_down"](hb)
+
+    ms = timed(block, max(3, args.steps // 2))
+    ops = sum(2.0 * Mb * K * N for _, K, N in shapes)
+    out["block_set_cfg3"] = {"config": "config 3: M=32760, r=64, QKV 5120->15360, out 5120->5120, "
+                                       "FFN-up 5120->27648, FFN-down 13824->5120 (bias, low-rank)",
+                             "ms": ms, "tops": ops / (ms * 1e-3) / 1e12}
+    return out
+
+
+def measured_peak(key: str):
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f).get(key)
+    except (OSError, ValueError):
+        return None
+
+
+def load_traffic(kind: str):
+    """DRAM bytes per launch from the committed ncu summary (profiles/traffic.json), when present."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(kind)
+    except (OSError, ValueError):
+        return None
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

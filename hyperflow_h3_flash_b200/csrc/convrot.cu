@@ -1,0 +1,388 @@
+// C ABI of the B200 INT8 convrot linear (declarations and contracts: include/convrot.h).
+//
+// One translation unit holds every kernel, so the device error word is a plain file-scope __device__ variable.
+// Host side: argument validation (shape, alignment, group), TMA tensor-map encoding through the driver entry
+// point (no libcuda link dependency), per-device lazy state (SM count, compute capability), and dispatch to the
+// template instances of rotate_quant_kernel and convrot_gemm_kernel.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/convrot.h"
+#include "gemm_sm100.cuh"
+#include "rotate_quant.cuh"
+
+namespace convrot {
+
+__device__ int g_error_word;  // CONVROT_ERR_TIMEOUT after a bounded wait expired; cleared by convrot_poll_error
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+uint64_t g_wait_limit_ns = 2000000000ull;
+
+struct DeviceState {
+  bool ready = false;
+  int status = CONVROT_OK;
+  int sms = 0;
+  int* error_word = nullptr;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceState g_devices[kMaxDevices];
+std::mutex g_mutex;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return CONVROT_ERR_CUDA;
+}
+
+// Per-device lazy set-up: architecture check, SM count, the address of the error word, the driver entry point.
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (dev < 0 || dev >= kMaxDevices) return CONVROT_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& st = g_devices[dev];
+  if (!st.ready) {
+    int major = 0, minor = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) return cuda_fail(e);
+    if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) return cuda_fail(e);
+    if ((e = cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return cuda_fail(e);
+    st.status = (major == 10 && minor == 0) ? CONVROT_OK : CONVROT_ERR_ARCH;
+    if (st.status == CONVROT_OK) {
+      if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.error_word), g_error_word)) != cudaSuccess)
+        return cuda_fail(e);
+      if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if ((e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q)) != cudaSuccess)
+          return cuda_fail(e);
+        if (q != cudaDriverEntryPointSuccess || !fn) return CONVROT_ERR_CUDA;
+        g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+      }
+    }
+    st.ready = true;
+  }
+  if (st.status != CONVROT_OK) return st.status;
+  *out = &st;
+  return CONVROT_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 2-D K-major tensor map: rows x cols elements of `elem` bytes, row pitch ld elements, box box_rows x box_cols,
+// swizzle matching box_cols * elem (128 or 64 bytes).
+int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem, int64_t rows, int64_t cols,
+             int64_t ld, int box_rows, int box_cols) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const int inner = box_cols * elem;
+  CUtensorMapSwizzle sw = inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return CONVROT_ERR_CUDA;
+  }
+  return CONVROT_OK;
+}
+
+template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
+int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
+                const CUtensorMap& tup, const GemmParams& p, cudaStream_t stream) {
+  auto kernel = convrot_gemm_kernel<Cfg, KIND, EPI, LR_ATOM, LR_ATOMS>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_fail(e);
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
+  const int grid = tiles < st.sms ? tiles : st.sms;
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+// ---------------------------------------------------------------------------------------------- GEMM dispatch
+
+using CfgI8 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 0, 0>;
+using CfgI8LR32 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 64, 1>;
+using CfgI8LR64 = GemmCfg<KIND_I8, 256, 3, EPI_DEQUANT, 128, 1>;
+using CfgRaw = GemmCfg<KIND_I8, 256, 4, EPI_RAW_I32, 0, 0>;
+
+int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+            const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
+            int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream) {
+  if (M < 0 || N <= 0 || K <= 0) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || N > (1 << 24)) return CONVROT_ERR_SHAPE;
+  if (!q || !w || !out) return CONVROT_ERR_ARG;
+  if (!raw && (!sx || !ws)) return CONVROT_ERR_ARG;
+  const bool has_lr = !raw && xa && up && r > 0;
+  if (!raw && (xa || up) && !has_lr) return CONVROT_ERR_ARG;
+  if (has_lr && r > 64) return CONVROT_ERR_SHAPE;
+  if (K % 16 || ldq < K || ldw < K || ldo < N) return CONVROT_ERR_SHAPE;
+  if (ldq % 16 || ldw % 16 || !aligned16(q) || !aligned16(w)) return CONVROT_ERR_ALIGN;
+  if (raw ? (ldo % 4 || !aligned16(out)) : (ldo % 8 || !aligned16(out))) return CONVROT_ERR_ALIGN;
+  if (!raw && (!aligned16(ws) || (bias && !aligned16(bias)))) return CONVROT_ERR_ALIGN;
+  if (has_lr && (ldxa < r || ld_up < r || ldxa % 8 || ld_up % 8 || !aligned16(xa) || !aligned16(up)))
+    return ldxa < r || ld_up < r ? CONVROT_ERR_SHAPE : CONVROT_ERR_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+
+  CUtensorMap ta, tb, txa, tup;
+  memset(&txa, 0, sizeof(txa));
+  memset(&tup, 0, sizeof(tup));
+  if ((rc = make_map(&ta, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, ldq, kBM, 128))) return rc;
+  if ((rc = make_map(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldw, 256, 128))) return rc;
+  const int lr_atom = r <= 32 ? 64 : 128;
+  if (has_lr) {
+    if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r, ldxa, kBM, lr_atom / 2))) return rc;
+    if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, 256, lr_atom / 2))) return rc;
+  }
+  GemmParams p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.sa = sx;
+  p.sb = ws;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.out = out;
+  p.ldo = ldo;
+  p.r = has_lr ? static_cast<int>(r) : 0;
+  p.wait_limit_ns = g_wait_limit_ns;
+  p.error_word = st->error_word;
+  if (raw) return launch_gemm<CfgRaw, KIND_I8, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, p, stream);
+  if (!has_lr) return launch_gemm<CfgI8, KIND_I8, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, p, stream);
+  if (lr_atom == 64) return launch_gemm<CfgI8LR32, KIND_I8, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, p, stream);
+  return launch_gemm<CfgI8LR64, KIND_I8, EPI_DEQUANT, 128, 1>(*st, ta, tb, txa, tup, p, stream);
+}
+
+// x . down^T -> bf16 [M, r] on kind::f16 tensor cores.
+template <int BN, int STAGES>
+using CfgDown = GemmCfg<KIND_BF16, BN, STAGES, EPI_BF16, 0, 0>;
+
+int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, int64_t M, int64_t K, int64_t r,
+                 void* xa, int64_t ldxa, cudaStream_t stream) {
+  if (M < 0 || K <= 0 || r <= 0) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  if (M > INT32_MAX || K > INT32_MAX || r > 256) return CONVROT_ERR_SHAPE;
+  if (!x || !down || !xa) return CONVROT_ERR_ARG;
+  if (K % 8 || ldx < K || ld_down < K || ldxa < r) return CONVROT_ERR_SHAPE;
+  if (ldx % 8 || ld_down % 8 || ldxa % 8 || !aligned16(x) || !aligned16(down) || !aligned16(xa))
+    return CONVROT_ERR_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int bn = r <= 32 ? 32 : r <= 64 ? 64 : r <= 128 ? 128 : 256;
+  CUtensorMap ta, tb, tz;
+  memset(&tz, 0, sizeof(tz));
+  if ((rc = make_map(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, kBM, 64))) return rc;
+  if ((rc = make_map(&tb, down, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, r, K, ld_down, bn, 64))) return rc;
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(r);
+  p.K = static_cast<int>(K);
+  p.out = xa;
+  p.ldo = ldxa;
+  p.wait_limit_ns = g_wait_limit_ns;
+  p.error_word = st->error_word;
+  switch (bn) {
+    case 32: return launch_gemm<CfgDown<32, 8>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    case 64: return launch_gemm<CfgDown<64, 8>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    case 128: return launch_gemm<CfgDown<128, 6>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    default: return launch_gemm<CfgDown<256, 4>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------- rotate+quant
+
+template <int G>
+int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t stream) {
+  const int nslots = p.K / 16;
+  int slots = 1;
+  while ((nslots + slots - 1) / slots > 512) slots *= 2;
+  if (slots > 4) return CONVROT_ERR_SHAPE;
+  int threads = (nslots + slots - 1) / slots;
+  threads = (threads + 31) / 32 * 32;
+  RotQuantParams q = p;
+  // Deepest row ring that leaves room for two CTAs per SM.
+  int stages = kRQMaxStages;
+  while (stages > 1 && rq_smem_bytes(p.K, threads, stages) > 110 * 1024) --stages;
+  q.stages = stages;
+  const size_t smem = rq_smem_bytes(p.K, threads, stages);
+  if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
+  int blocks_per_sm = 1;
+  cudaError_t e;
+  void (*kernel)(const RotQuantParams) = nullptr;
+  switch (slots) {
+    case 1: kernel = rotate_quant_kernel<G, 1>; break;
+    case 2: kernel = rotate_quant_kernel<G, 2>; break;
+    default: kernel = rotate_quant_kernel<G, 4>; break;
+  }
+  if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) !=
+      cudaSuccess)
+    return cuda_fail(e);
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, kernel, threads, smem)) != cudaSuccess)
+    return cuda_fail(e);
+  if (blocks_per_sm < 1) blocks_per_sm = 1;
+  int64_t grid = static_cast<int64_t>(st.sms) * blocks_per_sm;
+  if (grid > p.M) grid = p.M;
+  kernel<<<static_cast<int>(grid), threads, smem, stream>>>(q);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding, int8_t* q, int64_t ldq,
+                 float* s, cudaStream_t stream) {
+  if (M < 0 || K <= 0) return CONVROT_ERR_SHAPE;
+  if (group != 4 && group != 16 && group != 64 && group != 256) return CONVROT_ERR_GROUP;
+  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
+  if (K % group || K % 16 || K > 32768 || ldx < K || ldq < K || M > INT32_MAX) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  if (!x || !q || !s) return CONVROT_ERR_ARG;
+  if (ldx % 8 || ldq % 16 || !aligned16(x) || !aligned16(q)) return CONVROT_ERR_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  RotQuantParams p;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.q = q;
+  p.ldq = ldq;
+  p.s = s;
+  p.rounding = rounding;
+  p.stages = kRQMaxStages;
+  p.wait_limit_ns = g_wait_limit_ns;
+  p.error_word = st->error_word;
+  switch (group) {
+    case 4: return launch_rq<4>(*st, p, stream);
+    case 16: return launch_rq<16>(*st, p, stream);
+    case 64: return launch_rq<64>(*st, p, stream);
+    default: return launch_rq<256>(*st, p, stream);
+  }
+}
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+}  // namespace
+}  // namespace convrot
+
+using namespace convrot;
+
+extern "C" {
+
+int convrot_rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding, int8_t* q_out,
+                         int64_t ldq, float* s_out, const void* lr_down, int64_t ld_down, int64_t r, void* xa_out,
+                         int64_t ldxa, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = rotate_quant(x, ldx, M, K, group, rounding, q_out, ldq, s_out, s);
+  if (rc || !lr_down) return rc;
+  return lowrank_down(x, ldx, lr_down, ld_down, M, K, r, xa_out, ldxa, s);
+}
+
+int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down, int64_t M, int64_t K,
+                         int64_t r, void* xa_out, int64_t ldxa, void* stream) {
+  return lowrank_down(x, ldx, lr_down, ld_down, M, K, r, xa_out, ldxa, static_cast<cudaStream_t>(stream));
+}
+
+int convrot_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                 const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                 int64_t M, int64_t N, int64_t K, void* y, int64_t ldy, void* stream) {
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, ldy, false,
+                 static_cast<cudaStream_t>(stream));
+}
+
+int convrot_gemm_acc(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                     int32_t* acc, int64_t ldc, void* stream) {
+  return gemm_i8(q, ldq, w, ldw, nullptr, nullptr, nullptr, nullptr, 0, nullptr, 0, 0, M, N, K, acc, ldc, true,
+                 static_cast<cudaStream_t>(stream));
+}
+
+size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r) {
+  if (M < 0 || K < 0 || r < 0) return 0;
+  return align256(static_cast<size_t>(M) * K) + align256(static_cast<size_t>(M) * 4) +
+         align256(static_cast<size_t>(M) * r * 2);
+}
+
+int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* ws, const void* bias,
+                   const void* lr_down, int64_t ld_down, const void* lr_up, int64_t ld_up, int64_t r, int64_t M,
+                   int64_t N, int64_t K, int group, void* workspace, size_t workspace_bytes, void* y, int64_t ldy,
+                   void* stream) {
+  if (M < 0 || K <= 0 || r < 0) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  const bool has_lr = lr_down && lr_up && r > 0;
+  if ((lr_down || lr_up) && !has_lr) return CONVROT_ERR_ARG;
+  const int64_t rr = has_lr ? r : 0;
+  const int64_t ldxa = (rr + 7) / 8 * 8;
+  const int64_t ldq = (K + 15) / 16 * 16;
+  const size_t need = align256(static_cast<size_t>(M) * ldq) + align256(static_cast<size_t>(M) * 4) +
+                      align256(static_cast<size_t>(M) * ldxa * 2);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return CONVROT_ERR_ARG;
+  uint8_t* ws_bytes = static_cast<uint8_t*>(workspace);
+  int8_t* q = reinterpret_cast<int8_t*>(ws_bytes);
+  float* sx = reinterpret_cast<float*>(ws_bytes + align256(static_cast<size_t>(M) * ldq));
+  void* xa = ws_bytes + align256(static_cast<size_t>(M) * ldq) + align256(static_cast<size_t>(M) * 4);
+  int rc = convrot_rotate_quant(x, ldx, M, K, group, CONVROT_ROUND_KERNEL, q, ldq, sx, has_lr ? lr_down : nullptr,
+                                ld_down, rr, xa, ldxa, stream);
+  if (rc) return rc;
+  return convrot_gemm(q, ldq, w, ldw, sx, ws, bias, has_lr ? xa : nullptr, ldxa, has_lr ? lr_up : nullptr, ld_up, rr,
+                      M, N, K, y, ldy, stream);
+}
+
+const char* convrot_status_string(int status) {
+  switch (status) {
+    case CONVROT_OK: return "ok";
+    case CONVROT_ERR_SHAPE: return "unsupported or inconsistent shape";
+    case CONVROT_ERR_GROUP: return "unsupported Hadamard group (4, 16, 64 or 256)";
+    case CONVROT_ERR_ALIGN: return "pointer or leading dimension breaks the 16-byte alignment rules";
+    case CONVROT_ERR_CUDA: return "CUDA call failed";
+    case CONVROT_ERR_ARCH: return "device is not sm_100 (B200)";
+    case CONVROT_ERR_TIMEOUT: return "a kernel's bounded wait expired";
+    case CONVROT_ERR_ARG: return "missing pointer or unknown option";
+    default: return "unknown status";
+  }
+}
+
+int convrot_last_cuda_error(void) { return t_last_cuda_error; }
+
+int convrot_poll_error(void* stream) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int word = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&word, g_error_word, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  if (word) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_error_word, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return word;
+}
+
+void convrot_set_wait_limit_ns(uint64_t ns) { g_wait_limit_ns = ns ? ns : 2000000000ull; }
+
+int convrot_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,511 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a, with the convrot epilogues.
+//
+//   D[M, N] = A[M, K] . B[N, K]^T, both operands K-major (row-major with K contiguous), staged by TMA in 128-byte
+//   SWIZZLE_128B rows, accumulated in TMEM (two accumulator buffers so the epilogue of one tile overlaps the
+//   main loop of the next).
+//
+//   KIND_I8  : int8 x int8 -> int32 (tcgen05.mma kind::i8, K = 32 per instruction, 128 K per stage)
+//   KIND_BF16: bf16 x bf16 -> fp32  (tcgen05.mma kind::f16, K = 16 per instruction, 64 K per stage)
+//
+// Warp roles (one CTA per SM, CTAs stride over output tiles in row-major tile order):
+//   warp 0      TMA producer of the A/B ring
+//   warp 1      TMEM allocator; lane 0 issues every MMA and commit
+//   warps 2..5  epilogue: TMEM -> registers -> global, one 32-lane TMEM quadrant each
+//   warp 6      (low-rank only) TMA producer of the low-rank operand tiles
+//
+// Epilogues:
+//   EPI_DEQUANT   y = bf16((float(acc) * sa[m]) * sb[n] [+ bias[n]] [+ xa[m,:] . up[n,:]])   (int8.py:311, 324)
+//                 The low-rank term is a second, kind::f16 MMA (A = xa tile, B = up tile) that accumulates onto
+//                 the dequantised fp32 values the epilogue writes back into the same TMEM buffer.
+//   EPI_RAW_I32   acc as int32 (accumulator parity tests)
+//   EPI_BF16      y = bf16(acc_f32) (the low-rank down projection x . down^T)
+//
+// Every wait is bounded by a %globaltimer deadline; on expiry the CTA records CONVROT_ERR_TIMEOUT in a device
+// error word, drains its own TMA loads and MMAs (again bounded), frees its TMEM and returns.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "ptx.cuh"
+
+namespace convrot {
+
+enum { KIND_I8 = 0, KIND_BF16 = 1 };
+enum { EPI_DEQUANT = 0, EPI_RAW_I32 = 1, EPI_BF16 = 2 };
+
+struct GemmParams {
+  int M, N, K;
+  const float* sa;      // [M]   (EPI_DEQUANT)
+  const float* sb;      // [N]   (EPI_DEQUANT)
+  const __nv_bfloat16* bias;  // [N] or null
+  void* out;            // bf16 [M, N] or int32 [M, N]
+  int64_t ldo;          // elements
+  int r;                // low-rank width (0 = none)
+  uint64_t wait_limit_ns;
+  int* error_word;
+};
+
+constexpr int kBM = 128;
+constexpr int kRowBytes = 128;  // bytes of K per stage row (one SWIZZLE_128B atom)
+
+__host__ __device__ constexpr int tmem_cols_for(int bn) {
+  return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
+}
+
+// LR_ATOM: bytes of K per low-rank operand row atom (64 -> SWIZZLE_64B, 128 -> SWIZZLE_128B); LR_ATOMS atoms.
+template <int KIND, int BN, int STAGES, int EPI, int LR_ATOM, int LR_ATOMS>
+struct GemmCfg {
+  static constexpr int kBN = BN;
+  static constexpr int kStages = STAGES;
+  static constexpr bool kHasLR = (LR_ATOMS > 0);
+  static constexpr int kABytes = kBM * kRowBytes;
+  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kLRXaBytes = kHasLR ? kBM * LR_ATOM * LR_ATOMS : 0;
+  static constexpr int kLRUpBytes = kHasLR ? BN * LR_ATOM * LR_ATOMS : 0;
+  static constexpr int kMmaPerStage = 4;  // 32 bytes of K per MMA
+  static constexpr int kTmemCols = tmem_cols_for(BN);
+  static constexpr int kThreads = kHasLR ? 224 : 192;
+  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2], lr_done[2], lr_full, lr_empty, drain
+  static constexpr int kNumBars = 2 * STAGES + 8 + 3;
+  static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
+  static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes +
+                                    kBarBytes;
+  static constexpr uint32_t kIdesc = KIND == KIND_I8 ? make_idesc_i8(kBM, BN) : make_idesc_bf16(kBM, BN);
+  static constexpr uint32_t kIdescLR = make_idesc_bf16(kBM, BN);
+};
+
+__device__ __forceinline__ void record_error(int* word, int code) {
+  if (word) atomicCAS(word, 0, code);
+}
+
+template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
+    convrot_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const __grid_constant__ CUtensorMap tmap_xa, const __grid_constant__ CUtensorMap tmap_up,
+                        const GemmParams p) {
+  constexpr int BN = Cfg::kBN;
+  constexpr int S = Cfg::kStages;
+  constexpr bool HAS_LR = Cfg::kHasLR;
+  extern __shared__ __align__(1024) uint8_t gemm_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* lr_xa = ring + S * Cfg::kStageBytes;
+  uint8_t* lr_up = lr_xa + Cfg::kLRXaBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lr_up + Cfg::kLRUpBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tmem_full = bars + 2 * S;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* epi_ready = tmem_full + 4;
+  uint64_t* lr_done = tmem_full + 6;
+  uint64_t* lr_full = tmem_full + 8;
+  uint64_t* lr_empty = tmem_full + 9;
+  uint64_t* drain = tmem_full + 10;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nkb = (p.K * (KIND == KIND_I8 ? 1 : 2) + kRowBytes - 1) / kRowBytes;
+  constexpr int kKPerStage = KIND == KIND_I8 ? 128 : 64;  // elements
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 4);
+      mbar_init(&epi_ready[b], 4);
+      mbar_init(&lr_done[b], 1);
+    }
+    mbar_init(lr_full, 1);
+    mbar_init(lr_empty, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    if (HAS_LR) {
+      tma_prefetch_desc(&tmap_xa);
+      tma_prefetch_desc(&tmap_up);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc<Cfg::kTmemCols>(tmem_holder);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+  auto fail = [&]() {
+    *abort_flag = 1;
+    record_error(p.error_word, 6 /* CONVROT_ERR_TIMEOUT */);
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (A/B ring)
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;  // last load per stage, for draining after an abort
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / num_n) * kBM;
+        const int n0 = (tile % num_n) * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, limit, abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          uint8_t* sa_ptr = ring + stage * Cfg::kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sa_ptr, &tmap_a, &full[stage], kb * kKPerStage, m0);
+          tma_load_2d(sa_ptr + Cfg::kABytes, &tmap_b, &full[stage], kb * kKPerStage, n0);
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // let every load this thread issued land before the CTA leaves
+        volatile int never = 0;
+        for (int s = 0; s < S; ++s)
+          if (issued_mask >> s & 1) mbar_wait_bounded(&full[s], issued_parity >> s & 1, limit, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int pending_lr = -1;  // local tile index whose low-rank MMA is not issued yet
+      uint32_t lr_full_phase = 0;
+      const uint32_t ring_base = smem_u32(ring);
+      const uint32_t xa_base = smem_u32(lr_xa);
+      const uint32_t up_base = smem_u32(lr_up);
+      // Issues the low-rank MMA of local tile j: D[buf j] += xa_tile . up_tile^T (kind::f16, K = 16 per MMA).
+      auto issue_lr = [&](int j) {
+        const uint32_t d = tmem_base + (j & 1) * BN;
+        int kstep = 0;
+        for (int a = 0; a < LR_ATOMS; ++a) {
+          for (int off = 0; off < LR_ATOM; off += 32, ++kstep) {
+            const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
+            const uint64_t bd = make_kmajor_desc(up_base + a * BN * LR_ATOM + off, LR_ATOM);
+            mma_f16(d, ad, bd, Cfg::kIdescLR, 1u);
+          }
+        }
+        mma_commit(&lr_done[j & 1]);
+        mma_commit(lr_empty);
+      };
+      // Non-blocking: issue the pending low-rank MMA once its epilogue pass 1 and operands are in place.
+      auto try_lr = [&]() {
+        if (!HAS_LR || pending_lr < 0) return;
+        if (!mbar_try_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+        if (!mbar_try_wait(lr_full, lr_full_phase)) return;
+        tc_fence_after();
+        issue_lr(pending_lr);
+        lr_full_phase ^= 1;
+        pending_lr = -1;
+      };
+      auto flush_lr = [&]() -> bool {
+        if (!HAS_LR || pending_lr < 0) return true;
+        if (!mbar_wait_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag)) return false;
+        if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
+        tc_fence_after();
+        issue_lr(pending_lr);
+        lr_full_phase ^= 1;
+        pending_lr = -1;
+        return true;
+      };
+      int i = 0;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++i) {
+        const uint32_t buf = i & 1;
+        if (!mbar_wait_bounded(&tmem_empty[buf], ((i >> 1) & 1) ^ 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          // wait for the stage, issuing a pending low-rank MMA while the data is in flight
+          if (HAS_LR) {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t spin = 0; !mbar_try_wait(&full[stage], phase); ++spin) {
+              try_lr();
+              if ((spin & 63) == 63 && (*abort_flag || globaltimer_ns() - t0 > limit)) {
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
+          } else if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = ring_base + stage * Cfg::kStageBytes;
+          const uint32_t b_addr = a_addr + Cfg::kABytes;
+          const uint64_t ad = make_kmajor_desc(a_addr, kRowBytes);
+          const uint64_t bd = make_kmajor_desc(b_addr, kRowBytes);
+#pragma unroll
+          for (int kk = 0; kk < Cfg::kMmaPerStage; ++kk) {
+            // +32 bytes of K inside the 128-byte swizzle atom: +2 in the (addr >> 4) field
+            if (KIND == KIND_I8)
+              mma_i8(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
+            else
+              mma_f16(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (HAS_LR) try_lr();
+        }
+        if (!ok) break;
+        mma_commit(&tmem_full[buf]);
+        if (HAS_LR) {
+          if (!flush_lr()) {  // the previous tile's low-rank MMA must go before this one's
+            ok = false;
+            break;
+          }
+          pending_lr = i;
+        }
+      }
+      if (ok && !flush_lr()) ok = false;
+      if (!ok) fail();
+      // Make sure no MMA is still reading shared memory or writing TMEM when the CTA winds down.
+      mma_commit(drain);
+      volatile int never = 0;
+      mbar_wait_bounded(drain, 0, limit, &never);
+    }
+  } else if (HAS_LR && warp == 6) {
+    // ---------------------------------------------------------------- TMA producer (low-rank operand tiles)
+    if (lane == 0) {
+      bool loaded = false;
+      uint32_t loaded_parity = 0;
+      int i = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+        const int m0 = (tile / num_n) * kBM;
+        const int n0 = (tile % num_n) * BN;
+        // tile i reuses the operand buffer once the low-rank MMA of tile i-1 (phase i-1 of lr_empty) is done
+        if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
+          fail();
+          break;
+        }
+        mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
+        for (int a = 0; a < LR_ATOMS; ++a) {
+          tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, a * (LR_ATOM / 2), m0);
+          tma_load_2d(lr_up + a * BN * LR_ATOM, &tmap_up, lr_full, a * (LR_ATOM / 2), n0);
+        }
+        loaded = true;
+        loaded_parity = i & 1;
+      }
+      if (loaded && *abort_flag) {
+        volatile int never = 0;
+        mbar_wait_bounded(lr_full, loaded_parity, limit, &never);
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+      const uint32_t buf = i & 1;
+      const uint32_t par = (i >> 1) & 1;
+      const int m0 = (tile / num_n) * kBM;
+      const int n0 = (tile % num_n) * BN;
+      if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+
+      if (EPI == EPI_DEQUANT) {
+        const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_ld_wait();
+          const int n = n0 + c;
+          float sb[32], bias[32];
+          if (n + 32 <= p.N) {
+            const float4* s4 = reinterpret_cast<const float4*>(p.sb + n);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 f = __ldg(s4 + j);
+              sb[4 * j] = f.x;
+              sb[4 * j + 1] = f.y;
+              sb[4 * j + 2] = f.z;
+              sb[4 * j + 3] = f.w;
+            }
+            if (p.bias) {
+              const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint4 u = __ldg(b4 + j);
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  bias[8 * j + 2 * h] = __uint_as_float(w[h] << 16);
+                  bias[8 * j + 2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+                }
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const bool in = n + j < p.N;
+              sb[j] = in ? __ldg(p.sb + n + j) : 0.0f;
+              bias[j] = (in && p.bias) ? __bfloat162float(p.bias[n + j]) : 0.0f;
+            }
+          }
+          float t[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            // (float(acc) * sa) * sb, each product rounded to fp32 (no FMA contraction): int8.py:311, 324
+            float x = __fmul_rn(__int2float_rn(static_cast<int>(v[j])), sa);
+            x = __fmul_rn(x, sb[j]);
+            if (p.bias) x = __fadd_rn(x, bias[j]);
+            t[j] = x;
+          }
+          if (HAS_LR) {
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
+            tmem_st_32x32b_x32(taddr + c, w);
+          } else if (row_ok) {
+            __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
+            if (n + 32 <= p.N) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
+                packed[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(yrow);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) yrow[j] = __float2bfloat16_rn(t[j]);
+            }
+          }
+        }
+        if (HAS_LR) {
+          // pass 2: the low-rank MMA adds xa . up^T onto the fp32 values written above
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&epi_ready[buf]);
+          if (!mbar_wait_bounded(&lr_done[buf], par, limit, abort_flag)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            const int n = n0 + c;
+            if (!row_ok) continue;
+            __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
+            if (n + 32 <= p.N) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                packed[j] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(yrow);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) yrow[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            }
+          }
+        }
+      } else if (EPI == EPI_RAW_I32) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_ld_wait();
+          const int n = n0 + c;
+          if (!row_ok) continue;
+          int32_t* orow = reinterpret_cast<int32_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
+          if (n + 32 <= p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n + j < p.N) orow[j] = static_cast<int32_t>(v[j]);
+          }
+        }
+      } else {  // EPI_BF16
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_ld_wait();
+          const int n = n0 + c;
+          if (!row_ok) continue;
+          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
+          if (n + 32 <= p.N) {
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+              packed[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n + j < p.N) orow[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
+}  // namespace convrot

@@ -1,0 +1,288 @@
+// Fused online block-Hadamard rotation + per-token symmetric INT8 quantisation for sm_100a.
+//
+// Replaces the reference's `rotate_quant_kernel` / `rotate_quant_factored_kernel` (hyperflow_h3_flash,
+// src/hyperflow_h3_flash/int8.py:194-262, wrapper :326-344), and its torch path for short inputs (:173-178).
+//
+// Arithmetic.  y = x . blockdiag(H_G), H_G = kron(H4/2, ..., H4/2) = 2^-L H', H' = kron(H4', ...) with the
+// integer H4' = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]], H4' v = (v0+v1+v2+v3) - 2 reverse(v).
+// Every butterfly runs in fp64 on integer-form sums, so each partial sum is exact while the bf16 exponents of a
+// group span at most 45 - 2L binades (37 for G = 256, i.e. max|x| / min nonzero |x| < 2^37 inside a group):
+// y is the exact dot, rounded ONCE (to fp32 in the kernel mode, to bf16 in the torch mode).  Then
+//   kernel mode (int8.py:212-220): s = fp32(max(amax, 1e-12) / 127), inv = fp32(1 / s), q = rint(fp32(y * inv))
+//   torch  mode (int8.py:177-178): s = fp32(max(amax, 1e-12) / 127),                  q = rint(fp32(y / s))
+// with IEEE round-to-nearest divisions and products, rint = half to even, q clamped to +-127.
+//
+// Data flow (one CTA row at a time, rows striding by gridDim.x):
+//   * thread 0 streams whole rows into a ring of shared-memory buffers with bulk copies (cp.async.bulk), several
+//     rows ahead, so HBM sees deep queues without holding registers;
+//   * a team of T = G/16 threads owns one group, viewed as a T x 16 matrix X[a][b] (channel a*16 + b); each thread
+//     loads 16/T columns, applies H_T along a in registers, the team transposes through padded shared memory (fp64),
+//     and each thread then applies H16 along b to one row: it ends up with 16 CONTIGUOUS output channels;
+//   * row amax by warp shuffles + shared memory, then each thread quantises its 16 values and writes 16 bytes.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "ptx.cuh"
+
+namespace convrot {
+
+struct RotQuantParams {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  int M, K;
+  int8_t* q;
+  int64_t ldq;
+  float* s;
+  int rounding;  // 0 = kernel semantics, 1 = torch-path semantics
+  int stages;    // row buffers in flight, 1..kRQMaxStages
+  uint64_t wait_limit_ns;
+  int* error_word;
+};
+
+constexpr int kRQMaxStages = 4;
+constexpr int kRQPadDoubles = 2;  // 16-byte pad per transpose row: conflict-free 128-bit reads
+
+__device__ __forceinline__ void h4_int(double& a, double& b, double& c, double& d) {
+  const double s = (a + b) + (c + d);
+  const double na = fma(-2.0, d, s);
+  const double nb = fma(-2.0, c, s);
+  const double nc = fma(-2.0, b, s);
+  const double nd = fma(-2.0, a, s);
+  a = na;
+  b = nb;
+  c = nc;
+  d = nd;
+}
+
+// H16' on 16 values (index = 4 * hi + lo): H4' over lo, then over hi.
+__device__ __forceinline__ void h16_int(double (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 4; ++h) h4_int(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) h4_int(v[l], v[4 + l], v[8 + l], v[12 + l]);
+}
+
+__device__ __forceinline__ uint32_t pack4_codes(float a, float b, float c, float d) {
+  // a..d are already clamped to [-127, 127]; adding 1.5 * 2^23 rounds to an integer (half to even) and leaves the
+  // two's-complement code in the low byte.
+  const uint32_t ua = __float_as_uint(__fadd_rn(a, 12582912.0f));
+  const uint32_t ub = __float_as_uint(__fadd_rn(b, 12582912.0f));
+  const uint32_t uc = __float_as_uint(__fadd_rn(c, 12582912.0f));
+  const uint32_t ud = __float_as_uint(__fadd_rn(d, 12582912.0f));
+  return __byte_perm(__byte_perm(ua, ub, 0x0040), __byte_perm(uc, ud, 0x0040), 0x5410);
+}
+
+__device__ __forceinline__ float clamp127(float v) { return fminf(fmaxf(v, -127.0f), 127.0f); }
+
+__device__ __forceinline__ void record_error_rq(int* word) {
+  if (word) atomicCAS(word, 0, 6 /* CONVROT_ERR_TIMEOUT */);
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared memory: `stages` row buffers of K bf16 | transpose rows (blockDim * (16 + pad) doubles) |
+//                warp maxima (32 floats) | mbarriers.
+__host__ __device__ inline size_t rq_smem_bytes(int K, int threads, int stages) {
+  size_t rows = static_cast<size_t>(stages) * K * 2;
+  rows = (rows + 127) / 128 * 128;
+  size_t tr = static_cast<size_t>(threads) * (16 + kRQPadDoubles) * 8;
+  return rows + tr + 32 * 4 + kRQMaxStages * 8 + 64;
+}
+
+// G: group size (4, 16, 64, 256).  SLOTS: 16-channel slots per thread; blockDim is a multiple of 32 with
+// blockDim * SLOTS >= K / 16; threads whose slot lies beyond the row form whole idle teams.
+template <int G, int SLOTS>
+__global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams p) {
+  constexpr int T = G >= 16 ? G / 16 : 1;  // threads per group
+  constexpr int CPT = 16 / T;              // columns per thread in the column phase
+  constexpr int L = G == 4 ? 1 : G == 16 ? 2 : G == 64 ? 3 : 4;
+  constexpr double kScale = 1.0 / static_cast<double>(1 << L);  // 2^-L, exact
+
+  extern __shared__ __align__(1024) uint8_t rq_smem_raw[];
+  const int K = p.K;
+  const int nthr = blockDim.x;
+  const int stages = p.stages;
+  const int nslots = K / 16;
+  size_t rows_bytes = (static_cast<size_t>(stages) * K * 2 + 127) / 128 * 128;
+  __nv_bfloat16* rows = reinterpret_cast<__nv_bfloat16*>(rq_smem_raw);
+  double* tr = reinterpret_cast<double*>(rq_smem_raw + rows_bytes);
+  float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr) * (16 + kRQPadDoubles));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 32);
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = nthr >> 5;
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * 2;
+
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) {
+      const int m = blockIdx.x + st * gridDim.x;
+      if (m >= p.M) break;
+      mbar_arrive_expect_tx(&bars[st], row_bytes);
+      bulk_load(rows + static_cast<size_t>(st) * K, p.x + static_cast<int64_t>(m) * p.ldx, row_bytes, &bars[st]);
+    }
+  }
+
+  const int team_thread = tid % T;  // position in the group team (for G >= 64)
+  // Teams sync on their own lanes: a warp may hold one active and one idle team (slots beyond the row).
+  const unsigned team_mask = T >= 32 ? 0xffffffffu : (((1u << T) - 1u) << (lane & ~(T - 1)));
+  int it = 0;
+  bool aborted = false;
+  for (int m = blockIdx.x; m < p.M; m += gridDim.x, ++it) {
+    const int st = it % stages;
+    const uint32_t parity = (it / stages) & 1;
+    volatile int never = 0;
+    const bool arrived = mbar_wait_bounded(&bars[st], parity, p.wait_limit_ns, &never);
+    const __nv_bfloat16* xr = rows + static_cast<size_t>(st) * K;
+
+    float y[SLOTS][16];
+    float amax = 0.0f;
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl) {
+      const int slot = tid + sl * nthr;  // 16-channel slot: channels [16 slot, 16 slot + 16)
+      if (slot >= nslots) {  // team-uniform: nslots and nthr are multiples of the team size
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[sl][j] = 0.0f;
+        continue;
+      }
+      double v[16];
+      if constexpr (G == 4 || G == 16) {
+        const uint4* src = reinterpret_cast<const uint4*>(xr + slot * 16);
+        const uint4 u0 = src[0], u1 = src[1];
+        const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[2 * j] = static_cast<double>(__uint_as_float(w[j] << 16));
+          v[2 * j + 1] = static_cast<double>(__uint_as_float(w[j] & 0xffff0000u));
+        }
+        if constexpr (G == 4) {
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) h4_int(v[4 * gq], v[4 * gq + 1], v[4 * gq + 2], v[4 * gq + 3]);
+        } else {
+          h16_int(v);
+        }
+      } else {
+        // Column phase: this thread loads columns [team_thread * CPT, +CPT) of the T x 16 group matrix.
+        const int group_base = (slot - team_thread) * 16;  // first channel of the group
+        double c[T][CPT];
+#pragma unroll
+        for (int a = 0; a < T; ++a) {
+          const __nv_bfloat16* src = xr + group_base + a * 16 + team_thread * CPT;
+          if constexpr (CPT == 1) {
+            c[a][0] = static_cast<double>(__bfloat162float(src[0]));
+          } else {  // CPT == 4
+            const uint2 u = *reinterpret_cast<const uint2*>(src);
+            c[a][0] = static_cast<double>(__uint_as_float(u.x << 16));
+            c[a][1] = static_cast<double>(__uint_as_float(u.x & 0xffff0000u));
+            c[a][2] = static_cast<double>(__uint_as_float(u.y << 16));
+            c[a][3] = static_cast<double>(__uint_as_float(u.y & 0xffff0000u));
+          }
+        }
+        // H_T along a, per column
+#pragma unroll
+        for (int j = 0; j < CPT; ++j) {
+          if constexpr (T == 16) {
+            double col[16];
+#pragma unroll
+            for (int a = 0; a < 16; ++a) col[a] = c[a][j];
+            h16_int(col);
+#pragma unroll
+            for (int a = 0; a < 16; ++a) c[a][j] = col[a];
+          } else {  // T == 4
+            h4_int(c[0][j], c[1][j], c[2][j], c[3][j]);
+          }
+        }
+        // Transpose through shared memory: each thread owns one padded row of the team's T x 16 block; it writes
+        // its columns into every row, then reads back its own row.
+        double* team_buf = tr + static_cast<size_t>(tid - team_thread) * (16 + kRQPadDoubles);
+        __syncwarp(team_mask);
+#pragma unroll
+        for (int a = 0; a < T; ++a)
+#pragma unroll
+          for (int j = 0; j < CPT; ++j) team_buf[a * (16 + kRQPadDoubles) + team_thread * CPT + j] = c[a][j];
+        __syncwarp(team_mask);
+        const double2* rd = reinterpret_cast<const double2*>(team_buf + team_thread * (16 + kRQPadDoubles));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const double2 d2 = rd[j];
+          v[2 * j] = d2.x;
+          v[2 * j + 1] = d2.y;
+        }
+        __syncwarp(team_mask);
+        h16_int(v);
+      }
+      // Round the exact sums once.
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const double e = v[j] * kScale;
+        const float f = p.rounding == 0 ? __double2float_rn(e) : __bfloat162float(__double2bfloat16(e));
+        y[sl][j] = f;
+        amax = fmaxf(amax, fabsf(f));
+      }
+    }
+
+    // Row amax: warp shuffle, then across warps.  The barrier also agrees on a timed-out row copy.
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (lane == 0) warp_max[warp] = amax;
+    if (__syncthreads_or(!arrived)) {
+      if (tid == 0) record_error_rq(p.error_word);
+      aborted = true;
+      break;
+    }
+    float rmax = 0.0f;
+    for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
+    const float scale = __fdiv_rn(fmaxf(rmax, 1e-12f), 127.0f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    int8_t* qrow = p.q + static_cast<int64_t>(m) * p.ldq;
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl) {
+      const int slot = tid + sl * nthr;
+      if (slot >= nslots) continue;
+      float t[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        t[j] = clamp127(p.rounding == 0 ? __fmul_rn(y[sl][j], inv) : __fdiv_rn(y[sl][j], scale));
+      uint4 out;  // pack4_codes rounds half to even
+      out.x = pack4_codes(t[0], t[1], t[2], t[3]);
+      out.y = pack4_codes(t[4], t[5], t[6], t[7]);
+      out.z = pack4_codes(t[8], t[9], t[10], t[11]);
+      out.w = pack4_codes(t[12], t[13], t[14], t[15]);
+      *reinterpret_cast<uint4*>(qrow + slot * 16) = out;
+    }
+    if (tid == 0) p.s[m] = scale;
+    __syncthreads();  // the row buffer and warp maxima are free again
+    if (tid == 0) {
+      const int m_next = m + stages * gridDim.x;
+      if (m_next < p.M) {
+        mbar_arrive_expect_tx(&bars[st], row_bytes);
+        bulk_load(rows + static_cast<size_t>(st) * K, p.x + static_cast<int64_t>(m_next) * p.ldx, row_bytes,
+                  &bars[st]);
+      }
+    }
+  }
+  if (aborted && tid == 0) {
+    // Let the row copies still in flight land before the CTA leaves (bounded as well).
+    volatile int never = 0;
+    for (int k = 0; k < stages; ++k) {
+      const int j = it + k;
+      const int m = blockIdx.x + j * gridDim.x;
+      if (m >= p.M) break;
+      mbar_wait_bounded(&bars[j % stages], (j / stages) & 1, p.wait_limit_ns, &never);
+    }
+  }
+}
+
+}  // namespace convrot

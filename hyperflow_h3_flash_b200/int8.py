@@ -1,0 +1,335 @@
+"""INT8 W8A8 "convrot" linear on B200 (sm_100a): a drop-in for ``hyperflow_h3_flash.int8``.
+
+Same module API as the reference (src/hyperflow_h3_flash/int8.py): ``Int8RotLinear(in, out, group)`` with the state
+``{qweight int8 [N, K], wscale fp32 [N]}``, ``regular_hadamard``, ``hadamard_factors``, ``KERNEL_OPTIONS`` /
+``set_kernel_options``, ``resolve_int8_gemm`` and the kernel namespace ``_kernels()`` with
+``rotate_quant(x2, group) -> (q, s)`` and ``int8_matmul(a, b, sa, sb) -> bf16``.
+
+What runs on CUDA tensors: the hand-written sm_100a kernels of ``libconvrot.so`` (C ABI, include/convrot.h):
+
+* ``rotate_quant``: exact block-Hadamard rotation, rounded once to fp32, per-token ``s = max(amax, 1e-12) / 127``,
+  ``q = rint(y * (1/s))`` (int8.py:194-221);
+* ``int8_matmul``: a tcgen05 ``kind::i8`` GEMM with the ``(acc * sa) * sb -> bf16`` epilogue (int8.py:311, 324).
+
+Two optional extensions, off by default so existing checkpoints load unchanged: ``bias=True`` adds a bf16 ``bias``
+[N], and ``rank=r`` adds the low-rank correction ``up(down(x))`` of ``LowRankLinear`` (transformer.py:48-58) with
+``down.weight`` [r, K] and ``up.weight`` [N, r]. Both are fused into the GEMM epilogue.
+
+Rows: the reference sends CUDA inputs of fewer than ``_MIN_KERNEL_ROWS`` rows through its torch path, whose rotation
+is rounded to bf16 and whose codes divide by the scale (int8.py:164-167, 173-179). Here those rows run on the same CUDA
+kernels in that rounding mode, so both regimes reproduce the reference's numbers. CPU tensors take the reference's
+torch path, as in the reference. There is no other path: if the CUDA library is missing, CUDA inputs raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+from types import SimpleNamespace
+from typing import Any, ClassVar
+
+import torch
+from torch import Tensor, nn
+
+from . import _lib
+
+#: Run-time kernel choices of the reference; accepted for compatibility. Every choice runs the tcgen05 kernels.
+INT8_GEMMS = ("auto", "triton", "cublas", "sgl", "bf16")
+ROTATE_QUANTS = ("dense", "factored")
+
+#: Inputs with fewer rows reproduce the reference's torch-path rounding (int8.py:41-43, 164).
+_MIN_KERNEL_ROWS = 17
+
+#: Largest low-rank width fused into the GEMM epilogue.
+MAX_FUSED_RANK = 64
+
+KERNEL_OPTIONS: dict[str, Any] = {"int8_gemm": "auto", "rotate_quant": "dense"}
+
+
+def set_kernel_options(*, int8_gemm: str | None = None, rotate_quant: str | None = None) -> None:
+    """Validates and records the reference's kernel options (int8.py:49-57); they do not change the arithmetic."""
+    if int8_gemm is not None:
+        if int8_gemm not in INT8_GEMMS:
+            raise ValueError(f"int8_gemm must be one of {INT8_GEMMS}, got {int8_gemm!r}")
+        KERNEL_OPTIONS["int8_gemm"] = int8_gemm
+    if rotate_quant is not None:
+        if rotate_quant not in ROTATE_QUANTS:
+            raise ValueError(f"rotate_quant must be one of {ROTATE_QUANTS}, got {rotate_quant!r}")
+        KERNEL_OPTIONS["rotate_quant"] = rotate_quant
+
+
+def resolve_int8_gemm(device: torch.device) -> str:
+    """The GEMM that runs on ``device``: always the sm_100a tcgen05 kernel (int8.py:85-97 picks among backends)."""
+    return "tcgen05"
+
+
+@functools.cache
+def regular_hadamard(group: int) -> Tensor:
+    """``kron(H4/2, ..., H4/2)`` of size ``group`` (a power of 4), fp32: orthonormal, symmetric, rows sum to one
+    (int8.py:100-109). Raises ``ValueError`` for other sizes."""
+    h4 = torch.tensor([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=torch.float64) / 2
+    h, n = torch.ones(1, 1, dtype=torch.float64), 1
+    while n < group:
+        h, n = torch.kron(h, h4), n * 4
+    if n != group:
+        raise ValueError(f"Hadamard group {group} is not a power of 4")
+    return h.float()
+
+
+def hadamard_factors(group: int) -> tuple[int, int] | None:
+    """``(GA, GB)`` with ``regular_hadamard(group) == kron(regular_hadamard(GA), regular_hadamard(GB))``, both at
+    least 16; None otherwise (int8.py:112-119)."""
+    n = group.bit_length() - 1
+    if group < 256 or group != 1 << n or n % 2:
+        return None
+    ga = 4 ** (n // 4)
+    return ga, group // ga
+
+
+@functools.cache
+def _rotation(group: int, device: torch.device) -> Tensor:
+    return regular_hadamard(group).to(device=device, dtype=torch.bfloat16)
+
+
+class Int8RotLinear(nn.Module):
+    """W8A8 linear ``y = (q(x R) @ qweight^T) * s_x * wscale [+ bias] [+ up(down(x))]``, ``R = blockdiag(H_group)``.
+
+    The reference's constructor and state are unchanged (int8.py:127-148); ``bias`` and ``rank`` are keyword-only
+    extensions. Linears that read one input (``to_q``, ``to_k``, ``to_v``) quantise it once: a layer with
+    ``keep_input = True`` leaves its quantised input for the next layer, which reuses it if it receives the exact
+    same, unmodified tensor (int8.py:130-159).
+    """
+
+    _last_input: ClassVar[dict[str, Any]] = {}
+
+    def __init__(self, in_features: int, out_features: int, group: int, *, bias: bool = False,
+                 rank: int = 0) -> None:
+        super().__init__()
+        if in_features % group:
+            raise ValueError(f"in_features {in_features} is not a multiple of the Hadamard group {group}")
+        self.in_features, self.out_features, self.group = in_features, out_features, group
+        self.keep_input = False
+        # Parameters, not buffers: diffusers' streamed group offloading moves module buffers on but never back off.
+        self.qweight = nn.Parameter(torch.zeros(out_features, in_features, dtype=torch.int8), requires_grad=False)
+        self.wscale = nn.Parameter(torch.ones(out_features, dtype=torch.float32), requires_grad=False)
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_features, dtype=torch.bfloat16), requires_grad=False)
+        else:
+            self.register_parameter("bias", None)
+        self.rank = int(rank)
+        if self.rank:
+            self.down = nn.Linear(in_features, self.rank, bias=False, dtype=torch.bfloat16)
+            self.up = nn.Linear(self.rank, out_features, bias=False, dtype=torch.bfloat16)
+            self.down.weight.requires_grad_(False)
+            self.up.weight.requires_grad_(False)
+
+    def extra_repr(self) -> str:
+        extra = f", bias={self.bias is not None}, rank={self.rank}" if (self.bias is not None or self.rank) else ""
+        return f"in_features={self.in_features}, out_features={self.out_features}, group={self.group}{extra}"
+
+    def _quantize(self, x: Tensor, x2: Tensor, kernels: SimpleNamespace) -> tuple[Tensor, Tensor]:
+        cache = Int8RotLinear._last_input
+        # Inference tensors (`torch.inference_mode`) have no version counter.
+        version = None if x.is_inference() else x._version
+        hit = cache.get("x") is x and cache.get("version") == version and cache.get("group") == self.group
+        quantized = cache["value"] if hit else kernels.rotate_quant(x2, self.group)
+        cache.clear()
+        if self.keep_input:
+            cache.update(x=x, version=version, group=self.group, value=quantized)
+        return quantized
+
+    def forward(self, x: Tensor) -> Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
+        if x2.is_cuda:
+            kernels = _kernels()
+            if x2.shape[0] >= _MIN_KERNEL_ROWS:
+                xq, sx = self._quantize(x, x2, kernels)
+            else:
+                Int8RotLinear._last_input.clear()
+                xq, sx = kernels.rotate_quant_torch_rounding(x2, self.group)
+            xa = kernels.lowrank_down(x2, self.down.weight) if self.rank else None
+            y = kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
+                                       up=self.up.weight if self.rank else None)
+        else:
+            Int8RotLinear._last_input.clear()
+            y = self._forward_torch(x2, _rotation(self.group, x2.device))
+            if self.bias is not None:
+                y = y + self.bias
+            if self.rank:
+                y = y + self.up(self.down(x2))
+        return y.reshape(*shape[:-1], self.out_features).to(x.dtype)
+
+    def _forward_torch(self, x2: Tensor, rot: Tensor) -> Tensor:
+        """The reference's torch path (int8.py:173-179): the rotation is rounded to bf16 and the codes divide by
+        the scale. Used for CPU tensors only."""
+        g = self.group
+        xr = torch.matmul(x2.reshape(-1, self.in_features // g, g), rot).reshape(x2.shape).float()
+        sx = xr.abs().amax(1, keepdim=True).clamp_min(1e-12) / 127.0
+        xq = torch.clamp(torch.round(xr / sx), -127, 127)
+        acc = xq @ self.qweight.float().t()
+        return (acc * sx * self.wscale[None, :]).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------------------------------- kernels
+
+
+def _stream(t: Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _ptr(t: Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _require(t: Tensor, name: str, dtype: torch.dtype, ndim: int) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.dim() != ndim:
+        raise ValueError(f"{name} must be {ndim}-D, got shape {tuple(t.shape)}")
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must be contiguous in its last dimension")
+
+
+def _padded_k(K: int) -> int:
+    return -(-K // 16) * 16
+
+
+def _pad_cols(t: Tensor, cols: int) -> Tensor:
+    if t.shape[1] == cols and t.stride(0) % 16 == 0 and t.data_ptr() % 16 == 0:
+        return t
+    out = torch.zeros(t.shape[0], cols, dtype=t.dtype, device=t.device)
+    out[:, : t.shape[1]] = t
+    return out
+
+
+def rotate_quant(x: Tensor, group: int, rounding: int = _lib.ROUND_KERNEL) -> tuple[Tensor, Tensor]:
+    """``(q int8 [M, K], s fp32 [M])`` of the bf16 rows ``x`` (replaces int8.py:326-344)."""
+    _require(x, "x", torch.bfloat16, 2)
+    M, K = x.shape
+    if K % group:
+        raise ValueError(f"K = {K} is not a multiple of the Hadamard group {group}")
+    Kp = _padded_k(K)
+    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(0) % 8 or x.data_ptr() % 16) else x
+    q = torch.empty(M, Kp, dtype=torch.int8, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    rc = _lib.lib().convrot_rotate_quant(_ptr(xs), xs.stride(0), M, Kp, group, rounding, _ptr(q), Kp, _ptr(s),
+                                         None, 0, 0, None, 0, _stream(x))
+    _lib.check(rc, "convrot_rotate_quant")
+    return (q if Kp == K else q[:, :K]), s
+
+
+def rotate_quant_torch_rounding(x: Tensor, group: int) -> tuple[Tensor, Tensor]:
+    """``rotate_quant`` with the reference torch path's rounding (bf16 rotation, division): int8.py:175-178."""
+    return rotate_quant(x, group, _lib.ROUND_TORCH)
+
+
+def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
+    """``bf16(x . down^T)`` [M, r]: ``LowRankLinear.down`` (transformer.py:57-58) on kind::f16 tensor cores."""
+    _require(x, "x", torch.bfloat16, 2)
+    _require(down, "down", torch.bfloat16, 2)
+    M, K = x.shape
+    r = down.shape[0]
+    if down.shape[1] != K:
+        raise ValueError(f"down is {tuple(down.shape)}, expected [r, {K}]")
+    Kp = -(-K // 8) * 8
+    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(0) % 8 or x.data_ptr() % 16) else x
+    ds = _pad_cols(down.contiguous(), Kp) if (Kp != K or down.data_ptr() % 16) else down.contiguous()
+    ld = -(-r // 8) * 8
+    xa = torch.empty(M, ld, dtype=torch.bfloat16, device=x.device)
+    rc = _lib.lib().convrot_lowrank_down(_ptr(xs), xs.stride(0), _ptr(ds), ds.stride(0), M, Kp, r, _ptr(xa), ld,
+                                         _stream(x))
+    _lib.check(rc, "convrot_lowrank_down")
+    return xa if ld == r else xa[:, :r]
+
+
+def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor | None = None,
+                   xa: Tensor | None = None, up: Tensor | None = None) -> Tensor:
+    """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions)."""
+    _require(a, "a", torch.int8, 2)
+    _require(b, "b", torch.int8, 2)
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError(f"b is {tuple(b.shape)}, expected [N, {K}]")
+    sa = sa.reshape(-1).float().contiguous()
+    sb = sb.reshape(-1).float().contiguous()
+    if sa.numel() != M or sb.numel() != N:
+        raise ValueError("scale sizes do not match the operands")
+    Kp = _padded_k(K)
+    a_s = _pad_cols(a, Kp)
+    b_s = _pad_cols(b.contiguous(), Kp)
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.bfloat16).contiguous()
+        if bias.numel() != N:
+            raise ValueError("bias size does not match N")
+    r = 0
+    if xa is not None or up is not None:
+        if xa is None or up is None:
+            raise ValueError("the low-rank term needs both xa and up")
+        r = xa.shape[1]
+        if up.shape != (N, r):
+            raise ValueError(f"up is {tuple(up.shape)}, expected [{N}, {r}]")
+        if r > MAX_FUSED_RANK:
+            raise ValueError(f"low-rank width {r} exceeds the fused limit {MAX_FUSED_RANK}")
+        lr = -(-r // 8) * 8
+        xa = _pad_cols(xa.to(torch.bfloat16), lr)
+        up = _pad_cols(up.to(torch.bfloat16).contiguous(), lr)
+    ldy = -(-N // 8) * 8
+    y = torch.empty(M, ldy, dtype=torch.bfloat16, device=a.device)
+    rc = _lib.lib().convrot_gemm(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                 _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                 up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(y), ldy, _stream(a))
+    _lib.check(rc, "convrot_gemm")
+    return y if ldy == N else y[:, :N]
+
+
+def int8_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor) -> Tensor:
+    """``bf16((acc * sa) * sb)`` with ``acc = a . b^T`` (int8.py:376-390)."""
+    return convrot_matmul(a, b, sa, sb)
+
+
+def int8_mm_acc(a: Tensor, b: Tensor) -> Tensor:
+    """The raw int32 accumulator ``a . b^T`` of the same tcgen05 GEMM (what ``torch._int_mm`` gives, int8.py:362)."""
+    _require(a, "a", torch.int8, 2)
+    _require(b, "b", torch.int8, 2)
+    M, K = a.shape
+    N = b.shape[0]
+    Kp = _padded_k(K)
+    a_s = _pad_cols(a, Kp)
+    b_s = _pad_cols(b.contiguous(), Kp)
+    ldc = -(-N // 4) * 4
+    acc = torch.empty(M, ldc, dtype=torch.int32, device=a.device)
+    rc = _lib.lib().convrot_gemm_acc(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), M, N, Kp, _ptr(acc), ldc,
+                                     _stream(a))
+    _lib.check(rc, "convrot_gemm_acc")
+    return acc if ldc == N else acc[:, :N]
+
+
+@functools.cache
+def _kernels() -> SimpleNamespace:
+    """The kernel namespace the layers call (int8.py:182-398). Raises if ``libconvrot.so`` cannot be loaded."""
+    _lib.lib()
+    return SimpleNamespace(
+        rotate_quant=rotate_quant,
+        rotate_quant_torch_rounding=rotate_quant_torch_rounding,
+        int8_matmul=int8_matmul,
+        convrot_matmul=convrot_matmul,
+        lowrank_down=lowrank_down,
+        int8_mm_acc=int8_mm_acc,
+    )
+
+
+__all__ = [
+    "INT8_GEMMS",
+    "KERNEL_OPTIONS",
+    "MAX_FUSED_RANK",
+    "ROTATE_QUANTS",
+    "Int8RotLinear",
+    "hadamard_factors",
+    "regular_hadamard",
+    "resolve_int8_gemm",
+    "set_kernel_options",
+]

@@ -1,0 +1,135 @@
+/*
+ * convrot.h -- C ABI of the B200 (sm_100a) INT8 "convrot" linear.
+ *
+ * The functions replace the kernel namespace that the reference's `Int8RotLinear`
+ * calls into (hyperflow_h3_flash, src/hyperflow_h3_flash/int8.py):
+ *
+ *   convrot_rotate_quant  <- `rotate_quant(x2, group) -> (q, s)`         int8.py:326-344
+ *                            (kernels rotate_quant_kernel :194-221 and
+ *                             rotate_quant_factored_kernel :223-262)
+ *   convrot_gemm          <- `int8_matmul(a, b, sa, sb) -> bf16`         int8.py:376-390
+ *                            (int8_mm_kernel :283-313, or torch._int_mm +
+ *                             rescale_kernel :315-324, 353-364 on B200)
+ *                            plus a bias and the `up` half of LowRankLinear
+ *                            (transformer.py:48-58) fused into its epilogue
+ *   convrot_lowrank_down  <- `LowRankLinear.down(x)`                     transformer.py:57-58
+ *   convrot_linear        <- `Int8RotLinear.forward` kernel branch       int8.py:161-171
+ *
+ * Conventions
+ *   - Every pointer is a device pointer; every matrix is row-major with an explicit
+ *     leading dimension in ELEMENTS.  bf16 data is passed as `void*` (raw 16-bit
+ *     bfloat16 values).  `stream` is a `cudaStream_t` (NULL = legacy default stream).
+ *   - The caller allocates and owns every buffer.  The library keeps only a lazy
+ *     per-device cache (SM count, driver entry point), built on first use.
+ *   - Calls are stream-ordered and never synchronise the host.
+ *   - Every function returns a status (CONVROT_OK = 0); none aborts or throws.
+ *     `convrot_status_string` names a status.  CONVROT_ERR_CUDA carries the CUDA
+ *     error in `convrot_last_cuda_error()` (per host thread).
+ *   - M == 0 is a valid empty call: nothing is launched, CONVROT_OK is returned.
+ */
+#ifndef CONVROT_H_
+#define CONVROT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CONVROT_OK 0
+#define CONVROT_ERR_SHAPE 1       /* negative / too large M, N, K, r, or K % group != 0 */
+#define CONVROT_ERR_GROUP 2       /* group is not a supported power of 4 (4, 16, 64, 256) */
+#define CONVROT_ERR_ALIGN 3       /* a pointer or leading dimension breaks the 16-byte rules */
+#define CONVROT_ERR_CUDA 4        /* a CUDA runtime / driver call failed */
+#define CONVROT_ERR_ARCH 5        /* the current device is not sm_100 (B200 / GB200) */
+#define CONVROT_ERR_TIMEOUT 6     /* a kernel's bounded wait expired (see convrot_poll_error) */
+#define CONVROT_ERR_ARG 7         /* a required pointer is NULL or an option is unknown */
+
+/* Rotation arithmetic of convrot_rotate_quant. */
+#define CONVROT_ROUND_KERNEL 0 /* reference CUDA path (int8.py:194-221): exact dot rounded once to fp32,
+                                  q = rint(y * (1/scale)) */
+#define CONVROT_ROUND_TORCH 1  /* reference torch path (int8.py:173-178), used there for M < 17 rows:
+                                  exact dot rounded once to bf16, q = rint(y / scale) */
+
+/*
+ * Rotate + quantise (replaces int8.py:326-344).
+ *   x      bf16 [M, K], leading dimension ldx (elements)
+ *   q_out  int8 [M, K], leading dimension ldq; q = clamp(rint(y * inv), -127, 127)
+ *   s_out  fp32 [M];    s = max(amax_k |y[m,k]|, 1e-12) / 127, inv = 1 / s
+ * with y = x . blockdiag(H_group), H_group = kron(H4/2, ...) (int8.py:100-109).
+ * group in {4, 16, 64, 256}; K % group == 0 and K % 16 == 0; ldx, ldq multiples of 8 / 16;
+ * x, q_out 16-byte aligned.
+ * Low-rank (optional): if lr_down != NULL, also xa_out[m, j] = bf16(sum_k x[m,k] * lr_down[j,k]),
+ *   lr_down bf16 [r, K] (LowRankLinear.down.weight, leading dim ld_down), xa_out bf16 [M, r] (ldxa).
+ */
+int convrot_rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding,
+                         int8_t* q_out, int64_t ldq, float* s_out,
+                         const void* lr_down, int64_t ld_down, int64_t r, void* xa_out, int64_t ldxa,
+                         void* stream);
+
+/*
+ * Low-rank down projection alone: xa[m, j] = bf16(sum_k x[m,k] * lr_down[j,k]) (transformer.py:57-58).
+ * A tcgen05 bf16 GEMM with an fp32 accumulator; r % 16 == 0, 16 <= r <= 256, K % 8 == 0.
+ */
+int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down,
+                         int64_t M, int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
+
+/*
+ * INT8 GEMM with the dequantising epilogue (replaces int8.py:376-390):
+ *   y[m, n] = bf16( fp32(fp32(float(acc[m,n]) * sx[m]) * ws[n]) [+ bias[n]] [+ sum_j xa[m,j] * lr_up[n,j]] )
+ *   acc[m, n] = sum_k q[m,k] * w[n,k] (exact int32)
+ *   q int8 [M, K] (ldq), w int8 [N, K] (ldw, the reference's `qweight`), sx fp32 [M], ws fp32 [N] (`wscale`),
+ *   bias bf16 [N] or NULL, xa bf16 [M, r] (ldxa) and lr_up bf16 [N, r] (ld_up, LowRankLinear.up.weight) or NULL,
+ *   y bf16 [M, N] (ldy).
+ * Without bias and low-rank the output is bitwise the reference's (int8.py:311, 324).
+ * K % 16 == 0; ldq, ldw multiples of 16; ldy multiple of 8; r % 16 == 0 and r <= 256 when present.
+ */
+int convrot_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                 const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                 int64_t M, int64_t N, int64_t K, void* y, int64_t ldy, void* stream);
+
+/*
+ * The raw int32 accumulator acc = q . w^T of the same tcgen05 GEMM (no epilogue arithmetic); for parity tests
+ * of the accumulator (int8.py:306, 362: torch._int_mm).  acc int32 [M, N] (ldc multiple of 4).
+ */
+int convrot_gemm_acc(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, int64_t M, int64_t N,
+                     int64_t K, int32_t* acc, int64_t ldc, void* stream);
+
+/*
+ * Workspace for convrot_linear: q (int8 [M, K]), s (fp32 [M]) and xa (bf16 [M, r]), each 256-byte aligned.
+ */
+size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r);
+
+/*
+ * The whole layer (int8.py:161-171 kernel branch + bias + low-rank): rotate+quantise into `workspace`
+ * (convrot_workspace_size bytes, 256-byte aligned), then the GEMM.  Arguments as above.
+ */
+int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* ws, const void* bias,
+                   const void* lr_down, int64_t ld_down, const void* lr_up, int64_t ld_up, int64_t r,
+                   int64_t M, int64_t N, int64_t K, int group, void* workspace, size_t workspace_bytes,
+                   void* y, int64_t ldy, void* stream);
+
+/* Name of a status code. */
+const char* convrot_status_string(int status);
+
+/* The last CUDA error code seen by a call on this host thread (0 if none). */
+int convrot_last_cuda_error(void);
+
+/*
+ * Device-side error word of the current device: nonzero after a kernel's bounded wait expired
+ * (CONVROT_ERR_TIMEOUT); reading it synchronises `stream` and clears the word.
+ */
+int convrot_poll_error(void* stream);
+
+/* Bounded-wait limit of the GEMM kernels, in nanoseconds of %globaltimer (default 2e9). */
+void convrot_set_wait_limit_ns(uint64_t ns);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int convrot_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONVROT_H_ */

@@ -1,0 +1,93 @@
+"""The C ABI library (no GPU needed): it loads, exports every function include/convrot.h declares, and rejects bad
+arguments with the documented status codes before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "convrot.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from hyperflow_h3_flash_b200 import build
+
+    try:
+        build.build()
+    except (RuntimeError, OSError) as e:  # pragma: no cover - no toolkit
+        pytest.skip(f"cannot build libconvrot.so: {e}")
+    from hyperflow_h3_flash_b200 import _lib
+
+    return _lib
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(convrot_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_function_is_exported_and_bound(lib):
+    names = declared_functions()
+    assert len(names) >= 10
+    handle = ctypes.CDLL(os.path.join(ROOT, "hyperflow_h3_flash_b200", "libconvrot.so"))
+    for name in names:
+        assert hasattr(handle, name), name
+    assert sorted(lib.SIGNATURES) == names  # the Python binding covers exactly the header
+
+
+def test_status_strings_and_version(lib):
+    L = lib.lib()
+    for code in range(8):
+        assert L.convrot_status_string(code)
+    assert L.convrot_status_string(99) == b"unknown status"
+    assert L.convrot_version() >= 100
+
+
+def test_bad_arguments_are_rejected_before_any_device_call(lib):
+    L = lib.lib()
+    # group 32 is not a power of 4; group 128 is what the reference rejects too (int8.py:107-108)
+    for group in (2, 32, 128, 512):
+        rc = L.convrot_rotate_quant(None, 1024, 10, 1024, group, 0, None, 1024, None, None, 0, 0, None, 0, None)
+        assert rc == lib.ERR_GROUP
+    # K not a multiple of the group
+    assert L.convrot_rotate_quant(None, 1040, 10, 1040, 256, 0, None, 1040, None, None, 0, 0, None, 0,
+                                  None) == lib.ERR_SHAPE
+    # unknown rounding mode
+    assert L.convrot_rotate_quant(None, 1024, 10, 1024, 256, 7, None, 1024, None, None, 0, 0, None, 0,
+                                  None) == lib.ERR_ARG
+    # M == 0 is an empty, successful call
+    assert L.convrot_rotate_quant(None, 1024, 0, 1024, 256, 0, None, 1024, None, None, 0, 0, None, 0,
+                                  None) == lib.OK
+    assert L.convrot_gemm(None, 64, None, 64, None, None, None, None, 0, None, 0, 0, 0, 8, 64, None, 8,
+                          None) == lib.OK
+    # null operands, misaligned leading dimensions, K % 16, rank above the fused limit
+    assert L.convrot_gemm(None, 64, None, 64, None, None, None, None, 0, None, 0, 0, 4, 8, 64, None, 8,
+                          None) == lib.ERR_ARG
+    p = ctypes.c_void_p(4096)
+    assert L.convrot_gemm(p, 72, p, 64, p, p, None, None, 0, None, 0, 0, 4, 8, 64, p, 8, None) == lib.ERR_ALIGN
+    assert L.convrot_gemm(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 8, 40, p, 8, None) == lib.ERR_SHAPE
+    assert L.convrot_gemm(p, 64, p, 64, p, p, None, p, 128, p, 128, 128, 4, 8, 64, p, 8, None) == lib.ERR_SHAPE
+    assert L.convrot_lowrank_down(p, 64, p, 64, 4, 64, 300, p, 304, None) == lib.ERR_SHAPE
+
+
+def test_workspace_size(lib):
+    L = lib.lib()
+    M, K, r = 333, 5120, 32
+    a256 = lambda n: -(-n // 256) * 256  # noqa: E731
+    assert L.convrot_workspace_size(M, K, r) == a256(M * K) + a256(M * 4) + a256(M * r * 2)
+    assert L.convrot_workspace_size(-1, K, r) == 0
+
+
+def test_status_mapping_to_exceptions(lib):
+    with pytest.raises(ValueError, match="group"):
+        lib.check(lib.ERR_GROUP, "x")
+    with pytest.raises(lib.ConvrotError):
+        lib.check(lib.ERR_TIMEOUT, "x")
+    lib.check(lib.OK, "x")

@@ -1,0 +1,264 @@
+"""Parity of the sm_100a kernels with the CPU oracle (and with the reference's own kernels' golden outputs).
+
+Bit-exact: int8 codes, per-token scales, int32 accumulators, and the bias-free bf16 output (the reference's
+``(acc * sa) * sb`` epilogue, int8.py:311, 324). Within tolerance (no reference counterpart): the fused bias and
+low-rank output, max |err| / max |ref| <= 1e-2 and cosine >= 0.9999 against the composite reference
+``int8 + bias + up(down(x))``, and the low-rank ``x . down^T`` within one bf16 rounding plus the fp32
+accumulation bound.
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from hyperflow_h3_flash_b200 import _lib
+from hyperflow_h3_flash_b200 import int8 as I
+from hyperflow_h3_flash_b200 import synthetic
+from oracle import oracle as O
+from tests.conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def from_bits(b: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16)
+
+
+def edge_rows(x: torch.Tensor, group: int) -> torch.Tensor:
+    x = x.clone()
+    if x.shape[0] > 3:
+        x[1] = 0  # all-zero row: the 1e-12 floor of the scale
+        x[2, :group] = 0  # an all-zero group
+        x[3, 5] = 3.0e4  # a large outlier (amax far above the rest)
+    return x
+
+
+def close(out: np.ndarray, ref: np.ndarray) -> tuple[float, float]:
+    out = out.astype(np.float64)
+    ref = ref.astype(np.float64)
+    err = np.abs(out - ref).max() / max(np.abs(ref).max(), 1e-30)
+    cos = (out * ref).sum() / np.sqrt((out * out).sum() * (ref * ref).sum())
+    return float(err), float(cos)
+
+
+@pytest.fixture(autouse=True)
+def _no_device_error():
+    yield
+    assert _lib.lib().convrot_poll_error(None) == 0
+
+
+# ---------------------------------------------------------------------------------------------- rotate + quantise
+
+
+@pytest.mark.parametrize("M,K,group", [
+    (1, 256, 256), (17, 1024, 256), (70, 1024, 256), (333, 4096, 256), (64, 5120, 256), (40, 13824, 256),
+    (33, 512, 16), (33, 1024, 64), (33, 64, 4), (5, 16384, 256), (3, 32768, 256), (129, 2048, 16),
+])
+def test_rotate_quant_is_bitwise_the_oracle(M, K, group):
+    x = edge_rows(synthetic.activations(M, K, seed=M + K), group)
+    q, s = I.rotate_quant(x.to(DEV), group)
+    q_ref, s_ref = O.rotate_quant(bits(x), group)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("group", [16, 64, 256])
+def test_rotate_quant_is_bitwise_the_reference_kernel(group):
+    t = np.load(os.path.join(GOLDEN, "triton_kernels.npz"))
+    q, s = I.rotate_quant(from_bits(t["x"]).to(DEV), group)
+    assert np.array_equal(q.cpu().numpy(), t[f"dense_exact_g{group}_q"])
+    assert np.array_equal(s.cpu().numpy(), t[f"dense_exact_g{group}_s"])
+    # and within the reference's own tolerance of its inexact-dot runs (tests/test_int8.py:113-116)
+    gq, gs = t[f"dense_fp32_g{group}_q"], t[f"dense_fp32_g{group}_s"]
+    np.testing.assert_allclose(s.cpu().numpy(), gs, rtol=1e-5, atol=0)
+    assert (q.cpu().numpy() != gq).mean() <= 1e-5
+
+
+@pytest.mark.parametrize("M,K,group", [(8, 1024, 256), (16, 512, 16), (3, 256, 64), (1, 5120, 256)])
+def test_torch_rounding_mode_is_bitwise_the_reference_cpu_path(M, K, group):
+    x = synthetic.activations(M, K, seed=11)
+    q, s = I.rotate_quant_torch_rounding(x.to(DEV), group)
+    q_ref, s_ref = O.rotate_quant_cpu(bits(x), group)
+    assert np.array_equal(s.cpu().numpy(), s_ref)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+
+
+# ---------------------------------------------------------------------------------------------- GEMM
+
+
+def codes(M, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+
+
+@pytest.mark.parametrize("M,N,K", [
+    (1, 256, 256), (17, 96, 512), (129, 300, 640), (300, 256, 14336), (256, 512, 5120), (333, 5120, 4096),
+    (200, 1000, 128), (128, 256, 16),
+])
+def test_int32_accumulator_is_bitwise_the_oracle(M, N, K):
+    a, b = codes(M, K, 1), codes(N, K, 2)
+    acc = I.int8_mm_acc(a.to(DEV), b.to(DEV))
+    assert np.array_equal(acc.cpu().numpy(), O.int8_gemm(a.numpy(), b.numpy()))
+
+
+@pytest.mark.parametrize("M,N,K", [(17, 96, 512), (129, 300, 640), (300, 256, 14336), (333, 5120, 4096)])
+def test_bf16_epilogue_is_bitwise_the_oracle(M, N, K):
+    a, b = codes(M, K, 3), codes(N, K, 4)
+    g = torch.Generator().manual_seed(5)
+    sa = torch.rand(M, generator=g) * 0.05 + 1e-4
+    sb = torch.rand(N, generator=g) * 1e-3 + 1e-6
+    y = I.int8_matmul(a.to(DEV), b.to(DEV), sa.to(DEV), sb.to(DEV))
+    ref = O.epilogue(O.int8_gemm(a.numpy(), b.numpy()), sa.numpy(), sb.numpy())
+    assert np.array_equal(bits(y), ref)
+
+
+def test_gemm_and_rescale_are_bitwise_the_reference_kernels():
+    t = np.load(os.path.join(GOLDEN, "triton_kernels.npz"))
+    dev = lambda k: torch.from_numpy(t[k]).to(DEV)  # noqa: E731
+    y = I.int8_matmul(dev("gemm_a"), dev("gemm_b"), dev("gemm_sa"), dev("gemm_sb"))
+    assert np.array_equal(bits(y), t["gemm_out"])
+    acc = I.int8_mm_acc(dev("gemm_a"), dev("gemm_b"))
+    assert np.array_equal(acc.cpu().numpy(), t["rescale_acc"])
+
+
+# ---------------------------------------------------------------------------------------------- low-rank + bias
+
+
+@pytest.mark.parametrize("M,K,r", [(40, 1024, 16), (333, 4096, 32), (256, 5120, 64), (17, 520, 48)])
+def test_lowrank_down_within_one_bf16_ulp(M, K, r):
+    x = synthetic.activations(M, K, seed=7)
+    g = torch.Generator().manual_seed(9)
+    down = (torch.randn(r, K, generator=g) * 0.01).to(torch.bfloat16)
+    xa = I.lowrank_down(x.to(DEV), down.to(DEV))
+    ref = O.bf16_to_f32(O.lowrank_down(bits(x), bits(down.t().contiguous())))
+    out = xa.float().cpu().numpy()
+    # one bf16 rounding of the result plus the fp32 accumulation bound K * 2^-24 * (|x| . |A|)
+    mag = np.abs(O.bf16_to_f32(bits(x))).astype(np.float64) @ np.abs(O.bf16_to_f32(bits(down.t().contiguous())))
+    bound = np.abs(ref) * 2.0**-7 + K * 2.0**-24 * mag
+    assert (np.abs(out - ref) <= bound).all()
+    assert (out == ref).mean() > 0.95  # almost every value is the correctly rounded one
+
+
+@pytest.mark.parametrize("M,K,N,r,group", [
+    (40, 1024, 256, 16, 256), (333, 4096, 5120, 32, 256), (256, 5120, 512, 64, 256), (17, 512, 300, 48, 16),
+    (130, 2048, 1000, 0, 64),
+])
+def test_fused_bias_and_low_rank_within_tolerance(M, K, N, r, group):
+    x = synthetic.activations(M, K, seed=13)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=group)
+    q, s = I.rotate_quant(x.to(DEV), group)
+    xa = I.lowrank_down(x.to(DEV), w.down.to(DEV)) if r else None
+    y = I.convrot_matmul(q, w.qweight.to(DEV), s, w.wscale.to(DEV), bias=w.bias.to(DEV), xa=xa,
+                         up=w.up.to(DEV) if r else None)
+    A = bits(w.down.t().contiguous()) if r else None
+    B = bits(w.up.t().contiguous()) if r else None
+    # against the oracle's fused epilogue (same fp32 formula) ...
+    o = O.convrot_linear(bits(x), w.qweight.numpy(), w.wscale.numpy(), group, bits(w.bias), A, B)
+    out = y.float().cpu().numpy()
+    err, cos = close(out, O.bf16_to_f32(o["out"]))
+    assert err <= 1e-2 and cos >= 0.9999, (err, cos)
+    # ... and against the composite of the reference's modules
+    ref = O.bf16_to_f32(O.composite_reference(bits(x), w.qweight.numpy(), w.wscale.numpy(), group, bits(w.bias), A, B))
+    err, cos = close(out, ref)
+    assert err <= 1e-2 and cos >= 0.9999, (err, cos)
+    # every value is within a couple of bf16 ulps of the oracle's fused value
+    o32 = O.bf16_to_f32(o["out"])
+    assert (np.abs(out - o32) <= np.abs(o32) * 2.0**-6 + 1e-3 * np.abs(o32).max()).all()
+
+
+# ---------------------------------------------------------------------------------------------- the layer
+
+
+@pytest.mark.parametrize("M", [8, 16, 17, 333])
+def test_layer_forward_matches_the_reference_regime(M):
+    K, N, G = 1024, 512, 256
+    x = synthetic.activations(M, K, seed=21)
+    w = synthetic.linear_weights(K, N, bias=False, group=G)
+    layer = I.Int8RotLinear(K, N, G)
+    synthetic.load_into(layer, w)
+    y = layer.to(DEV)(x.to(DEV))
+    if M >= I._MIN_KERNEL_ROWS:
+        q, s = O.rotate_quant(bits(x), G)  # the reference's CUDA-kernel arithmetic
+    else:
+        q, s = O.rotate_quant_cpu(bits(x), G)  # its torch path, used below 17 rows (int8.py:164-167)
+    ref = O.epilogue(O.int8_gemm(q, w.qweight.numpy()), s, w.wscale.numpy())
+    assert np.array_equal(bits(y), ref)
+
+
+def test_layer_with_bias_and_low_rank_matches_the_composite():
+    M, K, N, r, G = 257, 5120, 640, 32, 256
+    x = synthetic.activations(M, K, seed=3)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=G)
+    layer = I.Int8RotLinear(K, N, G, bias=True, rank=r)
+    synthetic.load_into(layer, w)
+    y = layer.to(DEV)(x.to(DEV).reshape(1, M, K))
+    assert y.shape == (1, M, N)
+    ref = O.bf16_to_f32(O.composite_reference(bits(x), w.qweight.numpy(), w.wscale.numpy(), G, bits(w.bias),
+                                              bits(w.down.t().contiguous()), bits(w.up.t().contiguous())))
+    err, cos = close(y.float().cpu().numpy().reshape(M, N), ref)
+    assert err <= 1e-2 and cos >= 0.9999, (err, cos)
+
+
+def test_q_k_v_share_one_quantization(monkeypatch):
+    # tests/test_int8.py:149-173 on this module's kernels
+    kernels = I._kernels()
+    calls = []
+    rotate_quant = kernels.rotate_quant
+    monkeypatch.setattr(kernels, "rotate_quant", lambda *a: calls.append(1) or rotate_quant(*a))
+
+    def layer(seed):
+        w = synthetic.linear_weights(1024, 512, bias=False, group=256, seed_offset=seed)
+        m = I.Int8RotLinear(1024, 512, 256)
+        synthetic.load_into(m, w)
+        return m.to(DEV)
+
+    to_q, to_k, to_v = layer(0), layer(1), layer(2)
+    x = synthetic.activations(1000, 1024).to(DEV)
+    to_q.keep_input = to_k.keep_input = True
+    shared = [to_q(x), to_k(x), to_v(x)]
+    assert len(calls) == 1 and not I.Int8RotLinear._last_input
+    to_q.keep_input = to_k.keep_input = False
+    separate = [to_q(x), to_k(x), to_v(x)]
+    assert len(calls) == 4
+    for a, b in zip(shared, separate, strict=True):
+        assert torch.equal(a, b)
+    to_q.keep_input = True
+    to_q(x)
+    x.mul_(2)
+    to_k(x)
+    to_q(x)
+    to_k(x.clone())
+    assert len(calls) == 8
+
+
+# ---------------------------------------------------------------------------------------------- full-size shapes
+
+
+@pytest.mark.parametrize("M,K,N", [(32768, 5120, 5120), (32761, 5120, 5120)])
+def test_full_size_sampled_rows_are_bitwise_the_oracle(M, K, N):
+    """BASELINE configs 2 and 5 (ragged tail): every output row is computed, sampled rows checked bit-exact."""
+    G = 256
+    x = synthetic.activations(M, K, seed=0)
+    w = synthetic.linear_weights(K, N, bias=False, group=G)
+    xd = x.to(DEV)
+    q, s = I.rotate_quant(xd, G)
+    y = I.int8_matmul(q, w.qweight.to(DEV), s, w.wscale.to(DEV))
+    rows = np.unique(np.concatenate([np.arange(4), np.arange(M - 4, M),
+                                     np.random.default_rng(0).integers(0, M, 24)]))
+    q_ref, s_ref = O.rotate_quant(bits(x[rows]), G)
+    assert np.array_equal(q[rows].cpu().numpy(), q_ref)
+    assert np.array_equal(s[rows].cpu().numpy(), s_ref)
+    ref = O.epilogue(O.int8_gemm(q_ref, w.qweight.numpy()), s_ref, w.wscale.numpy())
+    assert np.array_equal(bits(y[rows]), ref)
+    # size-independent check over all rows: the output's row norms are finite and the zero-free rows are nonzero
+    assert torch.isfinite(y.float()).all()
