@@ -47,6 +47,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--rows", type=int, default=32768, help="token rows per rank")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--case", choices=["gemm", "gemm_plain", "rotate", "down"], default=None,
+                    help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
     return ap.parse_args()
 
 
@@ -475,9 +477,43 @@ def load_traffic(kind: str):
         return None
 
 
+def run_case(args) -> None:
+    """One kernel alone on a small case, for `ncu -k regex:<kernel> -s 3 -c 1`; prints its CUDA-event time."""
+    import torch
+
+    from hyperflow_h3_flash_b200 import int8 as I
+    from hyperflow_h3_flash_b200 import synthetic
+
+    dev = torch.device("cuda", 0)
+    M = args.rows
+    x = synthetic.activations(M, K_DIM).to(dev)
+    w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP).to(dev)
+    q, s = I.rotate_quant(x, GROUP)
+    xa = I.lowrank_down(x, w.down)
+    fns = {
+        "gemm": lambda: I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up),
+        "gemm_plain": lambda: I.int8_matmul(q, w.qweight, s, w.wscale),
+        "rotate": lambda: I.rotate_quant(x, GROUP),
+        "down": lambda: I.lowrank_down(x, w.down),
+    }
+    fn = fns[args.case]
+    times = []
+    for i in range(6):
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        fn()
+        en.record()
+        en.synchronize()
+        if i >= 3:
+            times.append(st.elapsed_time(en))
+    print(json.dumps({"case": args.case, "rows": M, "ms": times}), flush=True)
+
+
 def main() -> None:
     args = parse()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
