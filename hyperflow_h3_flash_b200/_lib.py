@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_last_cuda_error": ([], _I),
     "convrot_poll_error": ([_P], _I),
     "convrot_set_wait_limit_ns": ([_U64], None),
+    "convrot_set_gemm_mode": ([_I], _I),
     "convrot_version": ([], _I),
 }
 

@@ -14,6 +14,7 @@
 
 #include "../../include/convrot.h"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_2sm.cuh"
 #include "rotate_quant.cuh"
 
 namespace convrot {
@@ -24,6 +25,7 @@ namespace {
 
 thread_local int t_last_cuda_error = 0;
 uint64_t g_wait_limit_ns = 2000000000ull;
+int g_gemm_mode = 0;  // 0 auto, 1 one-SM kernel, 2 two-SM kernel
 
 struct DeviceState {
   bool ready = false;
@@ -103,15 +105,82 @@ int make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int 
   return CONVROT_OK;
 }
 
+// Per-(device, kernel) launch facts computed once: the shared-memory opt-in and the resident CTAs / clusters.
+// Keyed by the kernel's address; a handful of instances exist, so a small linear table suffices.
+struct LaunchCache {
+  const void* fn;
+  int dev;
+  int resident;
+};
+constexpr int kLaunchCacheSize = 256;
+LaunchCache g_launch_cache[kLaunchCacheSize];
+int g_launch_cache_n = 0;
+
+int cached_resident(const void* fn, int* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  for (int i = 0; i < g_launch_cache_n; ++i)
+    if (g_launch_cache[i].fn == fn && g_launch_cache[i].dev == dev) {
+      *out = g_launch_cache[i].resident;
+      return CONVROT_OK;
+    }
+  *out = -1;
+  return CONVROT_OK;
+}
+
+void store_resident(const void* fn, int resident) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_launch_cache_n < kLaunchCacheSize) g_launch_cache[g_launch_cache_n++] = {fn, dev, resident};
+}
+
 template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
 int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
                 const CUtensorMap& tup, const GemmParams& p, cudaStream_t stream) {
   auto kernel = convrot_gemm_kernel<Cfg, KIND, EPI, LR_ATOM, LR_ATOMS>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-  if (e != cudaSuccess) return cuda_fail(e);
+  int resident = -1;
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &resident);
+  if (rc) return rc;
+  cudaError_t e;
+  if (resident < 0) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    store_resident(reinterpret_cast<const void*>(kernel), 1);
+  }
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
   const int grid = tiles < st.sms ? tiles : st.sms;
   kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
+int launch_gemm2(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
+                 const CUtensorMap& tup, const GemmParams& p, cudaStream_t stream) {
+  auto kernel = convrot_gemm2sm_kernel<Cfg, EPI, LR_ATOM, LR_ATOMS>;
+  const int pair_tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
+  int clusters = -1;
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &clusters);
+  if (rc) return rc;
+  cudaError_t e;
+  if (clusters < 0) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e);
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(2 * st.sms, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (clusters < 1) clusters = st.sms / 2;
+    store_resident(reinterpret_cast<const void*>(kernel), clusters);
+  }
+  const int pairs = pair_tiles < clusters ? pair_tiles : clusters;
+  kernel<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
   e = cudaGetLastError();
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
@@ -122,6 +191,9 @@ using CfgI8 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 0, 0>;
 using CfgI8LR32 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 64, 1>;
 using CfgI8LR64 = GemmCfg<KIND_I8, 256, 3, EPI_DEQUANT, 128, 1>;
 using CfgRaw = GemmCfg<KIND_I8, 256, 4, EPI_RAW_I32, 0, 0>;
+using Cfg2 = Gemm2Cfg<6, 0, 0>;
+using Cfg2LR32 = Gemm2Cfg<6, 64, 1>;
+using Cfg2LR64 = Gemm2Cfg<6, 128, 1>;
 
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
@@ -144,15 +216,18 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   int rc = device_state(&st);
   if (rc) return rc;
 
+  // The 2-SM kernel (256 x 256 per CTA pair) unless the rows fit one 128-row tile or a mode is forced.
+  const bool two_sm = g_gemm_mode == 2 || (g_gemm_mode == 0 && M > kBM);
+  const int b_rows = two_sm ? 128 : 256;  // B rows per CTA tile
   CUtensorMap ta, tb, txa, tup;
   memset(&txa, 0, sizeof(txa));
   memset(&tup, 0, sizeof(tup));
   if ((rc = make_map(&ta, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, ldq, kBM, 128))) return rc;
-  if ((rc = make_map(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldw, 256, 128))) return rc;
+  if ((rc = make_map(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldw, b_rows, 128))) return rc;
   const int lr_atom = r <= 32 ? 64 : 128;
   if (has_lr) {
     if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r, ldxa, kBM, lr_atom / 2))) return rc;
-    if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, 256, lr_atom / 2))) return rc;
+    if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, b_rows, lr_atom / 2))) return rc;
   }
   GemmParams p;
   p.M = static_cast<int>(M);
@@ -166,6 +241,12 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.r = has_lr ? static_cast<int>(r) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
+  if (two_sm) {
+    if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, p, stream);
+    if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, p, stream);
+    if (lr_atom == 64) return launch_gemm2<Cfg2LR32, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, p, stream);
+    return launch_gemm2<Cfg2LR64, EPI_DEQUANT, 128, 1>(*st, ta, tb, txa, tup, p, stream);
+  }
   if (raw) return launch_gemm<CfgRaw, KIND_I8, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, p, stream);
   if (!has_lr) return launch_gemm<CfgI8, KIND_I8, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, p, stream);
   if (lr_atom == 64) return launch_gemm<CfgI8LR32, KIND_I8, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, p, stream);
@@ -221,25 +302,32 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
   int threads = (nslots + slots - 1) / slots;
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
-  // Deepest row ring that leaves room for two CTAs per SM.
-  int stages = kRQMaxStages;
+  // Two row buffers per CTA (one landing while one is processed); fewer only if the row is very long.
+  int stages = 2;
   while (stages > 1 && rq_smem_bytes(p.K, threads, stages) > 110 * 1024) --stages;
   q.stages = stages;
   const size_t smem = rq_smem_bytes(p.K, threads, stages);
   if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
-  int blocks_per_sm = 1;
   cudaError_t e;
   void (*kernel)(const RotQuantParams) = nullptr;
+  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
   switch (slots) {
-    case 1: kernel = rotate_quant_kernel<G, 1>; break;
-    case 2: kernel = rotate_quant_kernel<G, 2>; break;
-    default: kernel = rotate_quant_kernel<G, 4>; break;
+    case 1: kernel = torch_rounding ? rotate_quant_kernel<G, 1, 1> : rotate_quant_kernel<G, 1, 0>; break;
+    case 2: kernel = torch_rounding ? rotate_quant_kernel<G, 2, 1> : rotate_quant_kernel<G, 2, 0>; break;
+    default: kernel = torch_rounding ? rotate_quant_kernel<G, 4, 1> : rotate_quant_kernel<G, 4, 0>; break;
   }
-  if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))) !=
-      cudaSuccess)
-    return cuda_fail(e);
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks_per_sm, kernel, threads, smem)) != cudaSuccess)
-    return cuda_fail(e);
+  // The opt-in covers the largest configuration once; residency depends on (threads, smem), i.e. on K.
+  int opted = -1;
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &opted);
+  if (rc) return rc;
+  if (opted < 0) {
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
+      return cuda_fail(e);
+    store_resident(reinterpret_cast<const void*>(kernel), 1);
+  }
+  int blocks_per_sm = static_cast<int>((228 * 1024) / (smem + 1024));
+  const int by_threads = 2048 / threads;
+  if (blocks_per_sm > by_threads) blocks_per_sm = by_threads;
   if (blocks_per_sm < 1) blocks_per_sm = 1;
   int64_t grid = static_cast<int64_t>(st.sms) * blocks_per_sm;
   if (grid > p.M) grid = p.M;
@@ -382,6 +470,12 @@ int convrot_poll_error(void* stream) {
 }
 
 void convrot_set_wait_limit_ns(uint64_t ns) { g_wait_limit_ns = ns ? ns : 2000000000ull; }
+
+int convrot_set_gemm_mode(int mode) {
+  if (mode < 0 || mode > 2) return CONVROT_ERR_ARG;
+  g_gemm_mode = mode;
+  return CONVROT_OK;
+}
 
 int convrot_version(void) { return 100; }
 

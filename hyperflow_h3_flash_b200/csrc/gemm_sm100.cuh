@@ -79,6 +79,70 @@ __device__ __forceinline__ void record_error(int* word, int code) {
   if (word) atomicCAS(word, 0, code);
 }
 
+// Dequantise 32 accumulator columns [n, n + 32) of one row: t = fp32(fp32(float(acc) * sa) * sb[n]) [+ bias[n]],
+// each product rounded to fp32 without FMA contraction (int8.py:311, 324).  Columns at or beyond N give 0.
+__device__ __forceinline__ void dequant_chunk(const uint32_t (&v)[32], float sa, const float* __restrict__ sbv,
+                                              const __nv_bfloat16* __restrict__ biasv, int n, int N, float (&t)[32]) {
+  float sb[32], bias[32];
+  if (n + 32 <= N) {
+    const float4* s4 = reinterpret_cast<const float4*>(sbv + n);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 f = __ldg(s4 + j);
+      sb[4 * j] = f.x;
+      sb[4 * j + 1] = f.y;
+      sb[4 * j + 2] = f.z;
+      sb[4 * j + 3] = f.w;
+    }
+    if (biasv) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(biasv + n);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = __ldg(b4 + j);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          bias[8 * j + 2 * h] = __uint_as_float(w[h] << 16);
+          bias[8 * j + 2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const bool in = n + j < N;
+      sb[j] = in ? __ldg(sbv + n + j) : 0.0f;
+      bias[j] = (in && biasv) ? __bfloat162float(biasv[n + j]) : 0.0f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = __fmul_rn(__int2float_rn(static_cast<int>(v[j])), sa);
+    x = __fmul_rn(x, sb[j]);
+    if (biasv) x = __fadd_rn(x, bias[j]);
+    t[j] = x;
+  }
+}
+
+// Round 32 fp32 values to bf16 (nearest even) and store them at dst[0..32) (columns n.. of a row, N columns).
+__device__ __forceinline__ void store_bf16_chunk(__nv_bfloat16* dst, const float (&t)[32], int n, int N) {
+  if (n + 32 <= N) {
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
+      packed[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n + j < N) dst[j] = __float2bfloat16_rn(t[j]);
+  }
+}
+
 template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
 __global__ void __launch_bounds__(Cfg::kThreads, 1)
     convrot_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -345,70 +409,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           tmem_ld_32x32b_x32(taddr + c, v);
           tmem_ld_wait();
           const int n = n0 + c;
-          float sb[32], bias[32];
-          if (n + 32 <= p.N) {
-            const float4* s4 = reinterpret_cast<const float4*>(p.sb + n);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float4 f = __ldg(s4 + j);
-              sb[4 * j] = f.x;
-              sb[4 * j + 1] = f.y;
-              sb[4 * j + 2] = f.z;
-              sb[4 * j + 3] = f.w;
-            }
-            if (p.bias) {
-              const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 u = __ldg(b4 + j);
-                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  bias[8 * j + 2 * h] = __uint_as_float(w[h] << 16);
-                  bias[8 * j + 2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
-                }
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const bool in = n + j < p.N;
-              sb[j] = in ? __ldg(p.sb + n + j) : 0.0f;
-              bias[j] = (in && p.bias) ? __bfloat162float(p.bias[n + j]) : 0.0f;
-            }
-          }
           float t[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            // (float(acc) * sa) * sb, each product rounded to fp32 (no FMA contraction): int8.py:311, 324
-            float x = __fmul_rn(__int2float_rn(static_cast<int>(v[j])), sa);
-            x = __fmul_rn(x, sb[j]);
-            if (p.bias) x = __fadd_rn(x, bias[j]);
-            t[j] = x;
-          }
+          dequant_chunk(v, sa, p.sb, p.bias, n, p.N, t);
           if (HAS_LR) {
             uint32_t w[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
           } else if (row_ok) {
-            __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
-            if (n + 32 <= p.N) {
-              uint32_t packed[16];
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(yrow);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < p.N) yrow[j] = __float2bfloat16_rn(t[j]);
-            }
+            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n, t, n,
+                             p.N);
           }
         }
         if (HAS_LR) {
@@ -427,25 +437,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             uint32_t v[32];
             tmem_ld_32x32b_x32(taddr + c, v);
             tmem_ld_wait();
-            const int n = n0 + c;
             if (!row_ok) continue;
-            __nv_bfloat16* yrow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
-            if (n + 32 <= p.N) {
-              uint32_t packed[16];
+            float t[32];
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-                packed[j] = *reinterpret_cast<uint32_t*>(&h);
-              }
-              uint4* dst = reinterpret_cast<uint4*>(yrow);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < p.N) yrow[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
-            }
+            for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
+            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n0 + c,
+                             t, n0 + c, p.N);
           }
         }
       } else if (EPI == EPI_RAW_I32) {
@@ -475,23 +472,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           tmem_ld_wait();
           const int n = n0 + c;
           if (!row_ok) continue;
-          __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
-          if (n + 32 <= p.N) {
-            uint32_t packed[16];
+          float t[32];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-              packed[j] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(orow);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n + j < p.N) orow[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
-          }
+          for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
+          store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n, t, n, p.N);
         }
       }
       tc_fence_before();

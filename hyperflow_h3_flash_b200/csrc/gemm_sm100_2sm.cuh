@@ -1,0 +1,478 @@
+// 2-SM (cta_group::2) tcgen05 INT8 GEMM for sm_100a: one CTA pair per 256 x 256 output tile.
+//
+// The pair shares the tensor-core instruction  D[256 x 256] (+)= A[256 x K] . B[256 x K]^T  (kind::i8, K = 32):
+// CTA r of the pair holds A rows [128 r, 128 r + 128) and B rows (output columns) [128 r, 128 r + 128) in its own
+// shared memory, and its own TMEM holds accumulator rows [128 r, 128 r + 128) x all 256 columns.  Per SM this moves
+// half the B bytes of the 1-SM 128 x 256 tile for the same MACs, which is what keeps shared memory below its
+// bandwidth limit.
+//
+// Roles per CTA (224 threads; warp 6 only with the low-rank term):
+//   warp 0      TMA producer: this CTA's A tile and B half, signalling the LEADER's full barrier (cta_group::2 load)
+//   warp 1      TMEM allocation for the pair; in the leader (rank 0), lane 0 issues every MMA and commit
+//   warps 2..5  epilogue over this CTA's 128 accumulator rows (as in the 1-SM kernel)
+//   warp 6      TMA producer of this CTA's low-rank tiles (xa rows, up rows)
+//
+// Cross-CTA signalling uses plain (non-multicast) operations only: TMA loads complete on the leader's barrier
+// through its cluster address, the leader commits MMA completion once per CTA, and the peer's epilogue arrives on
+// the leader's barriers remotely (mapa).  Every wait is bounded as in the 1-SM kernel.
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace convrot {
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait with cluster-scope acquire, for barriers that receive arrivals from the other CTA.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
+                                                          volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((spin & 63) == 63) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
+  }
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted on a barrier that may live in the
+// other CTA of the pair (cluster address).  No multicast: each CTA fetches its own bytes.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
+template <int NCOLS>
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* holder_smem) {  // one warp in each CTA of the pair
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder_smem)),
+               "n"(NCOLS)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+template <int NCOLS>
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(NCOLS) : "memory");
+}
+
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the barrier at `cluster_addr` (this CTA's or the peer's) when the pair's MMAs so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+template <int STAGES, int LR_ATOM, int LR_ATOMS>
+struct Gemm2Cfg {
+  static constexpr int kBN = 256;             // output columns per pair tile (= per CTA accumulator)
+  static constexpr int kBHalf = 128;          // B rows per CTA
+  static constexpr int kStages = STAGES;
+  static constexpr bool kHasLR = LR_ATOMS > 0;
+  static constexpr int kABytes = kBM * kRowBytes;      // 16 KB
+  static constexpr int kBBytes = kBHalf * kRowBytes;   // 16 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kLRXaBytes = kHasLR ? kBM * LR_ATOM * LR_ATOMS : 0;
+  static constexpr int kLRUpBytes = kHasLR ? kBHalf * LR_ATOM * LR_ATOMS : 0;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kThreads = kHasLR ? 224 : 192;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2], lr_done[2], lr_full, lr_empty, drain
+  static constexpr int kNumBars = 2 * STAGES + 8 + 3;
+  static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
+  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kBarBytes;
+  static constexpr uint32_t kIdesc = make_idesc_i8(256, 256);
+  static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 256);
+};
+
+template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
+    convrot_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_xa, const __grid_constant__ CUtensorMap tmap_up,
+                           const GemmParams p) {
+  constexpr int BN = Cfg::kBN;
+  constexpr int S = Cfg::kStages;
+  constexpr bool HAS_LR = Cfg::kHasLR;
+  extern __shared__ __align__(1024) uint8_t gemm2_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm2_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* lr_xa = ring + S * Cfg::kStageBytes;
+  uint8_t* lr_up = lr_xa + Cfg::kLRXaBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lr_up + Cfg::kLRUpBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tmem_full = bars + 2 * S;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* epi_ready = tmem_full + 4;
+  uint64_t* lr_done = tmem_full + 6;
+  uint64_t* lr_full = tmem_full + 8;
+  uint64_t* lr_empty = tmem_full + 9;
+  uint64_t* drain = tmem_full + 10;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (p.M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int nkb = (p.K + kRowBytes - 1) / kRowBytes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&epi_ready[b], 8);
+      mbar_init(&lr_done[b], 1);
+    }
+    mbar_init(lr_full, 1);
+    mbar_init(lr_empty, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    if (HAS_LR) {
+      tma_prefetch_desc(&tmap_xa);
+      tma_prefetch_desc(&tmap_up);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair<Cfg::kTmemCols>(tmem_holder);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated for the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint64_t limit = p.wait_limit_ns;
+  auto fail = [&]() {
+    *abort_flag = 1;
+    record_error(p.error_word, 6 /* CONVROT_ERR_TIMEOUT */);
+  };
+  // Cluster addresses of the leader's barriers (targets of TMA transaction bytes and of the peer's arrivals).
+  const uint32_t leader_full0 = mapa_shared(smem_u32(full), 0);
+  const uint32_t leader_tmem_empty0 = mapa_shared(smem_u32(tmem_empty), 0);
+  const uint32_t leader_epi_ready0 = mapa_shared(smem_u32(epi_ready), 0);
+  const uint32_t leader_lr_full = mapa_shared(smem_u32(lr_full), 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer: this CTA's A rows and B half
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
+        const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * Cfg::kBHalf;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, limit, abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          uint8_t* st_ptr = ring + stage * Cfg::kStageBytes;
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          const uint32_t bar = leader_full0 + stage * 8;
+          tma_load_2d_pair(st_ptr, &tmap_a, bar, kb * 128, m0);
+          tma_load_2d_pair(st_ptr + Cfg::kABytes, &tmap_b, bar, kb * 128, n0);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {  // let loads in flight land before the CTA leaves (their barrier may be the peer's)
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int pending_lr = -1;
+      uint32_t lr_full_phase = 0;
+      const uint32_t ring_base = smem_u32(ring);
+      const uint32_t xa_base = smem_u32(lr_xa);
+      const uint32_t up_base = smem_u32(lr_up);
+      const uint32_t empty_self = smem_u32(empty), empty_peer = mapa_shared(empty_self, 1);
+      const uint32_t tfull_self = smem_u32(tmem_full), tfull_peer = mapa_shared(tfull_self, 1);
+      const uint32_t lrdone_self = smem_u32(lr_done), lrdone_peer = mapa_shared(lrdone_self, 1);
+      const uint32_t lrempty_self = smem_u32(lr_empty), lrempty_peer = mapa_shared(lrempty_self, 1);
+      auto issue_lr = [&](int j) {
+        const uint32_t d = tmem_base + (j & 1) * BN;
+        for (int a = 0; a < LR_ATOMS; ++a) {
+          for (int off = 0; off < LR_ATOM; off += 32) {
+            const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
+            const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kBHalf * LR_ATOM + off, LR_ATOM);
+            mma_f16_pair(d, ad, bd, Cfg::kIdescLR, 1u);
+          }
+        }
+        mma_commit_pair(lrdone_self + (j & 1) * 8);
+        mma_commit_pair(lrdone_peer + (j & 1) * 8);
+        mma_commit_pair(lrempty_self);
+        mma_commit_pair(lrempty_peer);
+      };
+      auto try_lr = [&]() {
+        if (!HAS_LR || pending_lr < 0) return;
+        if (!mbar_try_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+        if (!mbar_try_wait(lr_full, lr_full_phase)) return;
+        tc_fence_after();
+        issue_lr(pending_lr);
+        lr_full_phase ^= 1;
+        pending_lr = -1;
+      };
+      auto flush_lr = [&]() -> bool {
+        if (!HAS_LR || pending_lr < 0) return true;
+        if (!mbar_wait_cluster_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
+          return false;
+        if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
+        tc_fence_after();
+        issue_lr(pending_lr);
+        lr_full_phase ^= 1;
+        pending_lr = -1;
+        return true;
+      };
+      int i = 0;
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
+        const uint32_t buf = i & 1;
+        if (!mbar_wait_cluster_bounded(&tmem_empty[buf], ((i >> 1) & 1) ^ 1, limit, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (HAS_LR) {
+            const uint64_t t0 = globaltimer_ns();
+            for (uint32_t spin = 0; !mbar_try_wait(&full[stage], phase); ++spin) {
+              try_lr();
+              if ((spin & 63) == 63 && (*abort_flag || globaltimer_ns() - t0 > limit)) {
+                ok = false;
+                break;
+              }
+            }
+            if (!ok) break;
+          } else if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = ring_base + stage * Cfg::kStageBytes;
+          const uint64_t ad = make_kmajor_desc(a_addr, kRowBytes);
+          const uint64_t bd = make_kmajor_desc(a_addr + Cfg::kABytes, kRowBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) mma_i8_pair(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
+          mma_commit_pair(empty_self + stage * 8);
+          mma_commit_pair(empty_peer + stage * 8);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (HAS_LR) try_lr();
+        }
+        if (!ok) break;
+        mma_commit_pair(tfull_self + buf * 8);
+        mma_commit_pair(tfull_peer + buf * 8);
+        if (HAS_LR) {
+          if (!flush_lr()) {
+            ok = false;
+            break;
+          }
+          pending_lr = i;
+        }
+      }
+      if (ok && !flush_lr()) ok = false;
+      if (!ok) fail();
+      mma_commit_pair(smem_u32(drain));
+      volatile int never = 0;
+      mbar_wait_bounded(drain, 0, limit, &never);
+    }
+  } else if (HAS_LR && warp == 6) {
+    // ------------------------------------------------------------ TMA producer: low-rank tiles of this CTA
+    if (lane == 0) {
+      int i = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
+        const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * Cfg::kBHalf;
+        if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
+          fail();
+          ok = false;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
+        for (int a = 0; a < LR_ATOMS; ++a) {
+          tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, a * (LR_ATOM / 2), m0);
+          tma_load_2d_pair(lr_up + a * Cfg::kBHalf * LR_ATOM, &tmap_up, leader_lr_full, a * (LR_ATOM / 2), n0);
+        }
+      }
+      if (!ok) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // ------------------------------------------------------------ epilogue over this CTA's 128 rows
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int i = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
+      const uint32_t buf = i & 1;
+      const uint32_t par = (i >> 1) & 1;
+      const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int n0 = (tile % num_n) * BN;
+      if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+      if (EPI == EPI_DEQUANT) {
+        const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_ld_wait();
+          const int n = n0 + c;
+          float t[32];
+          dequant_chunk(v, sa, p.sb, p.bias, n, p.N, t);
+          if (HAS_LR) {
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
+            tmem_st_32x32b_x32(taddr + c, w);
+          } else if (row_ok) {
+            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n, t,
+                             n, p.N);
+          }
+        }
+        if (HAS_LR) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(leader_epi_ready0 + buf * 8);
+          if (!mbar_wait_bounded(&lr_done[buf], par, limit, abort_flag)) {
+            fail();
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            if (!row_ok) continue;
+            float t[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
+            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n0 + c,
+                             t, n0 + c, p.N);
+          }
+        }
+      } else {  // EPI_RAW_I32
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(taddr + c, v);
+          tmem_ld_wait();
+          const int n = n0 + c;
+          if (!row_ok) continue;
+          int32_t* orow = reinterpret_cast<int32_t*>(p.out) + static_cast<int64_t>(row) * p.ldo + n;
+          if (n + 32 <= p.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n + j < p.N) orow[j] = static_cast<int32_t>(v[j]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(leader_tmem_empty0 + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while the pair may still touch its shared memory or TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
+}  // namespace convrot

@@ -34,7 +34,7 @@ struct RotQuantParams {
   int8_t* q;
   int64_t ldq;
   float* s;
-  int rounding;  // 0 = kernel semantics, 1 = torch-path semantics
+  int rounding;  // 0 = kernel semantics, 1 = torch-path semantics (selects the template instance)
   int stages;    // row buffers in flight, 1..kRQMaxStages
   uint64_t wait_limit_ns;
   int* error_word;
@@ -64,16 +64,14 @@ __device__ __forceinline__ void h16_int(double (&v)[16]) {
 }
 
 __device__ __forceinline__ uint32_t pack4_codes(float a, float b, float c, float d) {
-  // a..d are already clamped to [-127, 127]; adding 1.5 * 2^23 rounds to an integer (half to even) and leaves the
-  // two's-complement code in the low byte.
+  // |a..d| < 127.5: adding 1.5 * 2^23 rounds to an integer (half to even) and leaves the two's-complement code in
+  // the low byte.
   const uint32_t ua = __float_as_uint(__fadd_rn(a, 12582912.0f));
   const uint32_t ub = __float_as_uint(__fadd_rn(b, 12582912.0f));
   const uint32_t uc = __float_as_uint(__fadd_rn(c, 12582912.0f));
   const uint32_t ud = __float_as_uint(__fadd_rn(d, 12582912.0f));
   return __byte_perm(__byte_perm(ua, ub, 0x0040), __byte_perm(uc, ud, 0x0040), 0x5410);
 }
-
-__device__ __forceinline__ float clamp127(float v) { return fminf(fmaxf(v, -127.0f), 127.0f); }
 
 __device__ __forceinline__ void record_error_rq(int* word) {
   if (word) atomicCAS(word, 0, 6 /* CONVROT_ERR_TIMEOUT */);
@@ -97,12 +95,15 @@ __host__ __device__ inline size_t rq_smem_bytes(int K, int threads, int stages) 
 
 // G: group size (4, 16, 64, 256).  SLOTS: 16-channel slots per thread; blockDim is a multiple of 32 with
 // blockDim * SLOTS >= K / 16; threads whose slot lies beyond the row form whole idle teams.
-template <int G, int SLOTS>
+template <int G, int SLOTS, int ROUNDING>
 __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams p) {
   constexpr int T = G >= 16 ? G / 16 : 1;  // threads per group
   constexpr int CPT = 16 / T;              // columns per thread in the column phase
   constexpr int L = G == 4 ? 1 : G == 16 ? 2 : G == 64 ? 3 : 4;
-  constexpr double kScale = 1.0 / static_cast<double>(1 << L);  // 2^-L, exact
+  // y = 2^-L * Y with Y the integer-form sum.  fp32/bf16 rounding commutes with the power-of-two scale (results
+  // below 2^-126, where it would not, can neither reach the 1e-12 floor of amax nor a nonzero code), so Y is
+  // rounded and the 2^-L goes into the scale arithmetic: exact.
+  constexpr float kScale = 1.0f / static_cast<float>(1 << L);
 
   extern __shared__ __align__(1024) uint8_t rq_smem_raw[];
   const int K = p.K;
@@ -223,11 +224,14 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
         __syncwarp(team_mask);
         h16_int(v);
       }
-      // Round the exact sums once.
+      // Round the exact sums once (to fp32, or to bf16 in the torch-path mode).
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const double e = v[j] * kScale;
-        const float f = p.rounding == 0 ? __double2float_rn(e) : __bfloat162float(__double2bfloat16(e));
+        float f;
+        if constexpr (ROUNDING == 0)
+          f = __double2float_rn(v[j]);
+        else
+          f = __bfloat162float(__double2bfloat16(v[j]));
         y[sl][j] = f;
         amax = fmaxf(amax, fabsf(f));
       }
@@ -244,17 +248,25 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     }
     float rmax = 0.0f;
     for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
-    const float scale = __fdiv_rn(fmaxf(rmax, 1e-12f), 127.0f);
-    const float inv = __fdiv_rn(1.0f, scale);
+    const float scale = __fdiv_rn(fmaxf(__fmul_rn(rmax, kScale), 1e-12f), 127.0f);
+    // y * inv = Yf * (inv * 2^-L) and y / s = Yf / (s * 2^L): the power-of-two factors are exact
+    const float inv_y = __fmul_rn(__fdiv_rn(1.0f, scale), kScale);
+    const float scale_y = __fdiv_rn(scale, kScale);
     int8_t* qrow = p.q + static_cast<int64_t>(m) * p.ldq;
 #pragma unroll
     for (int sl = 0; sl < SLOTS; ++sl) {
       const int slot = tid + sl * nthr;
       if (slot >= nslots) continue;
+      // No clamp is needed: |y| <= amax gives |y * inv| <= 127 (1 + 2^-24) / (1 - 2^-24) < 127.5 (and likewise
+      // |y / s| < 127.5), so rint never leaves [-127, 127] for finite inputs.
       float t[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        t[j] = clamp127(p.rounding == 0 ? __fmul_rn(y[sl][j], inv) : __fdiv_rn(y[sl][j], scale));
+      for (int j = 0; j < 16; ++j) {
+        if constexpr (ROUNDING == 0)
+          t[j] = __fmul_rn(y[sl][j], inv_y);
+        else
+          t[j] = __fdiv_rn(y[sl][j], scale_y);
+      }
       uint4 out;  // pack4_codes rounds half to even
       out.x = pack4_codes(t[0], t[1], t[2], t[3]);
       out.y = pack4_codes(t[4], t[5], t[6], t[7]);

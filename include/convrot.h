@@ -125,6 +125,14 @@ int convrot_poll_error(void* stream);
 /* Bounded-wait limit of the GEMM kernels, in nanoseconds of %globaltimer (default 2e9). */
 void convrot_set_wait_limit_ns(uint64_t ns);
 
+/*
+ * Which INT8 GEMM kernel convrot_gemm / convrot_gemm_acc / convrot_linear launch: 0 = automatic (the 2-SM
+ * cta_group::2 kernel with 256 x 256 tiles per CTA pair when M > 128, else the 1-SM 128 x 256 kernel),
+ * 1 = always the 1-SM kernel, 2 = always the 2-SM kernel.  Both give bitwise identical results.
+ * Process-wide; returns CONVROT_ERR_ARG for other values.
+ */
+int convrot_set_gemm_mode(int mode);
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int convrot_version(void);
 

@@ -57,6 +57,14 @@ def _no_device_error():
     assert _lib.lib().convrot_poll_error(None) == 0
 
 
+@pytest.fixture(params=[1, 2], ids=["gemm1sm", "gemm2sm"])
+def gemm_mode(request):
+    """Runs a test on the 1-SM (128x256 tiles) and on the 2-SM (cta_group::2, 256x256 per CTA pair) kernel."""
+    _lib.check(_lib.lib().convrot_set_gemm_mode(request.param), "convrot_set_gemm_mode")
+    yield request.param
+    _lib.lib().convrot_set_gemm_mode(0)
+
+
 # ---------------------------------------------------------------------------------------------- rotate + quantise
 
 
@@ -105,14 +113,14 @@ def codes(M, K, seed):
     (1, 256, 256), (17, 96, 512), (129, 300, 640), (300, 256, 14336), (256, 512, 5120), (333, 5120, 4096),
     (200, 1000, 128), (128, 256, 16),
 ])
-def test_int32_accumulator_is_bitwise_the_oracle(M, N, K):
+def test_int32_accumulator_is_bitwise_the_oracle(M, N, K, gemm_mode):
     a, b = codes(M, K, 1), codes(N, K, 2)
     acc = I.int8_mm_acc(a.to(DEV), b.to(DEV))
     assert np.array_equal(acc.cpu().numpy(), O.int8_gemm(a.numpy(), b.numpy()))
 
 
 @pytest.mark.parametrize("M,N,K", [(17, 96, 512), (129, 300, 640), (300, 256, 14336), (333, 5120, 4096)])
-def test_bf16_epilogue_is_bitwise_the_oracle(M, N, K):
+def test_bf16_epilogue_is_bitwise_the_oracle(M, N, K, gemm_mode):
     a, b = codes(M, K, 3), codes(N, K, 4)
     g = torch.Generator().manual_seed(5)
     sa = torch.rand(M, generator=g) * 0.05 + 1e-4
@@ -122,7 +130,7 @@ def test_bf16_epilogue_is_bitwise_the_oracle(M, N, K):
     assert np.array_equal(bits(y), ref)
 
 
-def test_gemm_and_rescale_are_bitwise_the_reference_kernels():
+def test_gemm_and_rescale_are_bitwise_the_reference_kernels(gemm_mode):
     t = np.load(os.path.join(GOLDEN, "triton_kernels.npz"))
     dev = lambda k: torch.from_numpy(t[k]).to(DEV)  # noqa: E731
     y = I.int8_matmul(dev("gemm_a"), dev("gemm_b"), dev("gemm_sa"), dev("gemm_sb"))
@@ -153,7 +161,7 @@ def test_lowrank_down_within_one_bf16_ulp(M, K, r):
     (40, 1024, 256, 16, 256), (333, 4096, 5120, 32, 256), (256, 5120, 512, 64, 256), (17, 512, 300, 48, 16),
     (130, 2048, 1000, 0, 64),
 ])
-def test_fused_bias_and_low_rank_within_tolerance(M, K, N, r, group):
+def test_fused_bias_and_low_rank_within_tolerance(M, K, N, r, group, gemm_mode):
     x = synthetic.activations(M, K, seed=13)
     w = synthetic.linear_weights(K, N, rank=r, bias=True, group=group)
     q, s = I.rotate_quant(x.to(DEV), group)
@@ -245,7 +253,7 @@ def test_q_k_v_share_one_quantization(monkeypatch):
 
 
 @pytest.mark.parametrize("M,K,N", [(32768, 5120, 5120), (32761, 5120, 5120)])
-def test_full_size_sampled_rows_are_bitwise_the_oracle(M, K, N):
+def test_full_size_sampled_rows_are_bitwise_the_oracle(M, K, N, gemm_mode):
     """BASELINE configs 2 and 5 (ragged tail): every output row is computed, sampled rows checked bit-exact."""
     G = 256
     x = synthetic.activations(M, K, seed=0)
@@ -262,3 +270,24 @@ def test_full_size_sampled_rows_are_bitwise_the_oracle(M, K, N):
     assert np.array_equal(bits(y[rows]), ref)
     # size-independent check over all rows: the output's row norms are finite and the zero-free rows are nonzero
     assert torch.isfinite(y.float()).all()
+
+
+@pytest.mark.parametrize("M,N,K,r", [(4096, 5120, 5120, 32), (1000, 15360, 5120, 64), (777, 5120, 13824, 64)])
+def test_one_and_two_sm_kernels_agree_bitwise(M, N, K, r):
+    """The 2-SM kernel changes the tiling, not the arithmetic: outputs equal the 1-SM kernel's bit for bit."""
+    x = synthetic.activations(M, K, seed=31).to(DEV)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256).to(DEV)
+    q, s = I.rotate_quant(x, 256)
+    xa = I.lowrank_down(x, w.down)
+    outs = []
+    for mode in (1, 2):
+        _lib.check(_lib.lib().convrot_set_gemm_mode(mode), "mode")
+        try:
+            outs.append((I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up),
+                         I.int8_mm_acc(q, w.qweight)))
+        finally:
+            _lib.lib().convrot_set_gemm_mode(0)
+    assert torch.equal(outs[0][1], outs[1][1])
+    # the low-rank MMA accumulates 256 vs 128 rows per instruction: allow the fp32 accumulation order to differ
+    a, b = outs[0][0].float(), outs[1][0].float()
+    assert ((a - b).abs() <= a.abs() * 2.0**-7 + 1e-2 * a.abs().max()).all()
