@@ -286,6 +286,7 @@ def run_ours(args) -> None:
 
     to_q, to_k, to_v, to_out = (make_layer(i, K_DIM, N_DIM, RANK) for i in range(4))
     to_q.keep_input = to_k.keep_input = True
+    I.share_lowrank(to_q, to_k, to_v)
     x_host = synthetic.activations(M, K_DIM, seed=rank).pin_memory()
     x = x_host.to(dev)
     y_host = torch.empty(M, N_DIM, dtype=torch.bfloat16).pin_memory()

@@ -31,6 +31,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_poll_error": ([_P], _I),
     "convrot_set_wait_limit_ns": ([_U64], None),
     "convrot_set_gemm_mode": ([_I], _I),
+    "convrot_set_rotate_variant": ([_I], _I),
+    "convrot_set_rotate_tuning": ([_I, _I], _I),
     "convrot_version": ([], _I),
 }
 

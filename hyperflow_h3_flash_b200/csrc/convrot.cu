@@ -26,6 +26,8 @@ namespace {
 thread_local int t_last_cuda_error = 0;
 uint64_t g_wait_limit_ns = 2000000000ull;
 int g_gemm_mode = 0;  // 0 auto, 1 one-SM kernel, 2 two-SM kernel
+int g_rq_variant = 0;  // G = 256 rotation: 0 two-column team kernel, 1 one-column kernel
+int g_rq_stages = 0, g_rq_blocks = 0;  // rotation tuning overrides (0 = automatic)
 
 struct DeviceState {
   bool ready = false;
@@ -150,8 +152,11 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
     if (e != cudaSuccess) return cuda_fail(e);
     store_resident(reinterpret_cast<const void*>(kernel), 1);
   }
+  // Kernels whose shared memory and TMEM leave room run two CTAs per SM (the low-rank down projection is
+  // HBM-bound with few tiles: two per SM keeps every tile of a 32k-row input in flight at once).
+  const int per_sm = (Cfg::kSmemBytes <= 113 * 1024 && Cfg::kTmemCols <= 256) ? 2 : 1;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
-  const int grid = tiles < st.sms ? tiles : st.sms;
+  const int grid = tiles < per_sm * st.sms ? tiles : per_sm * st.sms;
   kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
   e = cudaGetLastError();
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
@@ -284,9 +289,9 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   switch (bn) {
-    case 32: return launch_gemm<CfgDown<32, 8>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
-    case 64: return launch_gemm<CfgDown<64, 8>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
-    case 128: return launch_gemm<CfgDown<128, 6>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    case 32: return launch_gemm<CfgDown<32, 5>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    case 64: return launch_gemm<CfgDown<64, 4>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
+    case 128: return launch_gemm<CfgDown<128, 3>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
     default: return launch_gemm<CfgDown<256, 4>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
   }
 }
@@ -302,9 +307,21 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
   int threads = (nslots + slots - 1) / slots;
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
-  // Two row buffers per CTA (one landing while one is processed); fewer only if the row is very long.
-  int stages = 2;
-  while (stages > 1 && rq_smem_bytes(p.K, threads, stages) > 110 * 1024) --stages;
+  // Resident CTAs first (registers ~64 per thread), then the deepest row ring that fits beside them; the grid
+  // is oversubscribed 4x so that the last rows spread evenly (measured on B200 for K = 13824).
+  const int regs_per_thread = slots == 1 ? 64 : 128;
+  int resident = 65536 / (threads * regs_per_thread);
+  if (resident > 2048 / threads) resident = 2048 / threads;
+  if (resident < 1) resident = 1;
+  int stages = 1;
+  for (int st_try = 2; st_try <= kRQMaxStages; ++st_try) {
+    const size_t sm = rq_smem_bytes(p.K, threads, st_try);
+    if (sm > 227 * 1024 || static_cast<size_t>(resident) * (sm + 1024) > 228 * 1024) break;
+    stages = st_try;
+  }
+  int best_blocks = 4 * resident;
+  if (g_rq_stages > 0) stages = g_rq_stages;
+  if (g_rq_blocks > 0) best_blocks = g_rq_blocks;
   q.stages = stages;
   const size_t smem = rq_smem_bytes(p.K, threads, stages);
   if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
@@ -325,11 +342,57 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
       return cuda_fail(e);
     store_resident(reinterpret_cast<const void*>(kernel), 1);
   }
-  int blocks_per_sm = static_cast<int>((228 * 1024) / (smem + 1024));
-  const int by_threads = 2048 / threads;
-  if (blocks_per_sm > by_threads) blocks_per_sm = by_threads;
-  if (blocks_per_sm < 1) blocks_per_sm = 1;
-  int64_t grid = static_cast<int64_t>(st.sms) * blocks_per_sm;
+  int64_t grid = static_cast<int64_t>(st.sms) * best_blocks;
+  if (grid > p.M) grid = p.M;
+  kernel<<<static_cast<int>(grid), threads, smem, stream>>>(q);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+// G = 256: the two-column team kernel (8 threads per group).
+int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t stream) {
+  const int ngroups = p.K / 256;
+  int slots = 1;
+  while ((ngroups * 8 + slots - 1) / slots > 512) slots *= 2;
+  if (slots > 2) return CONVROT_ERR_SHAPE;
+  int threads = (ngroups * 8 + slots - 1) / slots;
+  threads = (threads + 31) / 32 * 32;
+  RotQuantParams q = p;
+  // The per-row work is a serial chain (exact rotation, block-wide amax, quantise), so throughput comes from
+  // resident CTAs: fill the SM with as many CTAs as registers allow (~96 per thread), then give each the deepest
+  // row ring that still fits (measured on B200: K = 5120 -> 4 CTAs x 3 row buffers).
+  const int regs_per_thread = slots == 1 ? 96 : 128;
+  int best_blocks = 65536 / (threads * regs_per_thread);
+  if (best_blocks > 2048 / threads) best_blocks = 2048 / threads;
+  if (best_blocks < 1) best_blocks = 1;
+  int best_stages = 1;
+  for (int stages = 2; stages <= kRQMaxStages; ++stages) {
+    const size_t sm = rq256_smem_bytes(p.K, threads, stages);
+    if (sm > 227 * 1024 || static_cast<size_t>(best_blocks) * (sm + 1024) > 228 * 1024) break;
+    best_stages = stages;
+  }
+  if (best_stages < 2) best_stages = 2;
+  q.stages = best_stages;
+  if (g_rq_stages > 0) q.stages = g_rq_stages;
+  if (g_rq_blocks > 0) best_blocks = g_rq_blocks;
+  const size_t smem = rq256_smem_bytes(p.K, threads, q.stages);
+  if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
+  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
+  void (*kernel)(const RotQuantParams) = nullptr;
+  if (slots == 1)
+    kernel = torch_rounding ? rotate_quant256_kernel<1, 1> : rotate_quant256_kernel<1, 0>;
+  else
+    kernel = torch_rounding ? rotate_quant256_kernel<2, 1> : rotate_quant256_kernel<2, 0>;
+  int opted = -1;
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &opted);
+  if (rc) return rc;
+  cudaError_t e;
+  if (opted < 0) {
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
+      return cuda_fail(e);
+    store_resident(reinterpret_cast<const void*>(kernel), 1);
+  }
+  int64_t grid = static_cast<int64_t>(st.sms) * best_blocks;
   if (grid > p.M) grid = p.M;
   kernel<<<static_cast<int>(grid), threads, smem, stream>>>(q);
   e = cudaGetLastError();
@@ -364,7 +427,13 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
     case 4: return launch_rq<4>(*st, p, stream);
     case 16: return launch_rq<16>(*st, p, stream);
     case 64: return launch_rq<64>(*st, p, stream);
-    default: return launch_rq<256>(*st, p, stream);
+    default: {
+      // The two-column kernel while a row needs at most 256 threads (K <= 8192); beyond, the one-column kernel
+      // keeps more rows resident per SM (measured: K = 13824 -> 0.58 ms vs 0.80 ms).
+      const bool two_col = g_rq_variant == 0 && (K / 256) * 8 <= 256;
+      if (g_rq_variant == 2) return launch_rq256(*st, p, stream);
+      return two_col ? launch_rq256(*st, p, stream) : launch_rq<256>(*st, p, stream);
+    }
   }
 }
 
@@ -470,6 +539,19 @@ int convrot_poll_error(void* stream) {
 }
 
 void convrot_set_wait_limit_ns(uint64_t ns) { g_wait_limit_ns = ns ? ns : 2000000000ull; }
+
+int convrot_set_rotate_tuning(int stages, int ctas_per_sm) {
+  if (stages < 0 || stages > kRQMaxStages || ctas_per_sm < 0 || ctas_per_sm > 32) return CONVROT_ERR_ARG;
+  g_rq_stages = stages;
+  g_rq_blocks = ctas_per_sm;
+  return CONVROT_OK;
+}
+
+int convrot_set_rotate_variant(int variant) {
+  if (variant < 0 || variant > 2) return CONVROT_ERR_ARG;
+  g_rq_variant = variant;
+  return CONVROT_OK;
+}
 
 int convrot_set_gemm_mode(int mode) {
   if (mode < 0 || mode > 2) return CONVROT_ERR_ARG;

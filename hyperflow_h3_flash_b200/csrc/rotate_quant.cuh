@@ -40,7 +40,7 @@ struct RotQuantParams {
   int* error_word;
 };
 
-constexpr int kRQMaxStages = 4;
+constexpr int kRQMaxStages = 8;
 constexpr int kRQPadDoubles = 2;  // 16-byte pad per transpose row: conflict-free 128-bit reads
 
 __device__ __forceinline__ void h4_int(double& a, double& b, double& c, double& d) {
@@ -287,6 +287,183 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
   }
   if (aborted && tid == 0) {
     // Let the row copies still in flight land before the CTA leaves (bounded as well).
+    volatile int never = 0;
+    for (int k = 0; k < stages; ++k) {
+      const int j = it + k;
+      const int m = blockIdx.x + j * gridDim.x;
+      if (m >= p.M) break;
+      mbar_wait_bounded(&bars[j % stages], (j / stages) & 1, p.wait_limit_ns, &never);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// G = 256 kernel: a team of 8 threads per group, two columns per thread.
+//
+// The row lands in shared memory as one bulk copy per group, each into a 544-byte slot (512 + 32 bytes of pad), so
+// the four teams of a warp read disjoint banks.  Thread tt of a team loads the bf16 pair (columns 2tt, 2tt+1) of
+// every row a of the 16 x 16 group matrix (16 32-bit loads for 32 values), applies H16 along a to both columns, and
+// the team transposes through shared memory in two halves (rows 0-7, then 8-15; 128-bit stores and loads): thread
+// tt ends up with rows tt and tt+8, i.e. channels [16 tt, 16 tt + 16) and [16 (tt+8), ...) of the group, applies H16
+// along b, and writes 2 x 16 contiguous codes.
+constexpr int kSlotBytes = 544;
+constexpr int kTrRow = 16 + kRQPadDoubles;  // doubles per transpose row
+
+__host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages) {
+  const size_t slots = static_cast<size_t>(K / 256) * kSlotBytes;
+  const size_t tr = static_cast<size_t>(threads / 8) * 8 * kTrRow * 8;  // per team: 8 rows of the half transpose
+  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + 64;
+}
+
+template <int SLOTS, int ROUNDING>
+__global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantParams p) {
+  extern __shared__ __align__(1024) uint8_t rq2_smem_raw[];
+  const int K = p.K;
+  const int ngroups = K / 256;
+  const int nthr = blockDim.x;
+  const int stages = p.stages;
+  const size_t stage_bytes = static_cast<size_t>(ngroups) * kSlotBytes;
+  uint8_t* rows = rq2_smem_raw;
+  double* tr = reinterpret_cast<double*>(rq2_smem_raw + stages * stage_bytes);
+  float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr / 8) * 8 * kTrRow);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 32);
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nwarps = nthr >> 5;
+  const int tt = tid & 7;                              // thread in team
+  const unsigned team_mask = 0xffu << (lane & ~7);     // the team's 8 lanes
+  double* team_buf = tr + static_cast<size_t>(tid >> 3) * 8 * kTrRow;
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * 2;
+  constexpr float kScale = 1.0f / 16.0f;  // 2^-L, L = 4
+
+  auto issue_row = [&](int stage, int m) {
+    // one bulk copy per group into its padded slot; all complete on the stage's barrier
+    mbar_arrive_expect_tx(&bars[stage], row_bytes);
+    const __nv_bfloat16* src = p.x + static_cast<int64_t>(m) * p.ldx;
+    uint8_t* dst = rows + stage * stage_bytes;
+    for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlotBytes, src + g * 256, 512, &bars[stage]);
+  };
+
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int st = 0; st < stages; ++st) {
+      const int m = blockIdx.x + st * gridDim.x;
+      if (m >= p.M) break;
+      issue_row(st, m);
+    }
+
+  int it = 0;
+  bool aborted = false;
+  for (int m = blockIdx.x; m < p.M; m += gridDim.x, ++it) {
+    const int st = it % stages;
+    volatile int never = 0;
+    const bool arrived = mbar_wait_bounded(&bars[st], (it / stages) & 1, p.wait_limit_ns, &never);
+    const uint8_t* xr = rows + st * stage_bytes;
+
+    float y[SLOTS][32];
+    float amax = 0.0f;
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl) {
+      const int g = (tid + sl * nthr) >> 3;  // group of this team (team-uniform)
+      if (g >= ngroups) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[sl][j] = 0.0f;
+        continue;
+      }
+      // column phase: columns 2tt and 2tt+1 of the 16 x 16 group matrix
+      double c0[16], c1[16];
+      const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlotBytes) + tt;
+#pragma unroll
+      for (int a = 0; a < 16; ++a) {
+        const uint32_t w = col[a * 8];
+        c0[a] = static_cast<double>(__uint_as_float(w << 16));
+        c1[a] = static_cast<double>(__uint_as_float(w & 0xffff0000u));
+      }
+      h16_int(c0);
+      h16_int(c1);
+      // transpose in two halves: rows [8h, 8h + 8) go through the team buffer, thread tt takes row 8h + tt
+      double v[2][16];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        __syncwarp(team_mask);
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+          *reinterpret_cast<double2*>(team_buf + a * kTrRow + 2 * tt) = make_double2(c0[8 * h + a], c1[8 * h + a]);
+        __syncwarp(team_mask);
+        const double2* rd = reinterpret_cast<const double2*>(team_buf + tt * kTrRow);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const double2 d2 = rd[j];
+          v[h][2 * j] = d2.x;
+          v[h][2 * j + 1] = d2.y;
+        }
+      }
+      h16_int(v[0]);
+      h16_int(v[1]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float f;
+          if constexpr (ROUNDING == 0)
+            f = __double2float_rn(v[h][j]);
+          else
+            f = __bfloat162float(__double2bfloat16(v[h][j]));
+          y[sl][16 * h + j] = f;
+          amax = fmaxf(amax, fabsf(f));
+        }
+    }
+
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (lane == 0) warp_max[warp] = amax;
+    if (__syncthreads_or(!arrived)) {
+      if (tid == 0) record_error_rq(p.error_word);
+      aborted = true;
+      break;
+    }
+    float rmax = 0.0f;
+    for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
+    const float scale = __fdiv_rn(fmaxf(__fmul_rn(rmax, kScale), 1e-12f), 127.0f);
+    const float inv_y = __fmul_rn(__fdiv_rn(1.0f, scale), kScale);
+    const float scale_y = __fdiv_rn(scale, kScale);
+    int8_t* qrow = p.q + static_cast<int64_t>(m) * p.ldq;
+#pragma unroll
+    for (int sl = 0; sl < SLOTS; ++sl) {
+      const int g = (tid + sl * nthr) >> 3;
+      if (g >= ngroups) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float t[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if constexpr (ROUNDING == 0)
+            t[j] = __fmul_rn(y[sl][16 * h + j], inv_y);
+          else
+            t[j] = __fdiv_rn(y[sl][16 * h + j], scale_y);
+        }
+        uint4 out;
+        out.x = pack4_codes(t[0], t[1], t[2], t[3]);
+        out.y = pack4_codes(t[4], t[5], t[6], t[7]);
+        out.z = pack4_codes(t[8], t[9], t[10], t[11]);
+        out.w = pack4_codes(t[12], t[13], t[14], t[15]);
+        *reinterpret_cast<uint4*>(qrow + g * 256 + (8 * h + tt) * 16) = out;
+      }
+    }
+    if (tid == 0) p.s[m] = scale;
+    __syncthreads();
+    if (tid == 0) {
+      const int m_next = m + stages * gridDim.x;
+      if (m_next < p.M) issue_row(st, m_next);
+    }
+  }
+  if (aborted && tid == 0) {
     volatile int never = 0;
     for (int k = 0; k < stages; ++k) {
       const int j = it + k;

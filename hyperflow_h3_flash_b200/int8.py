@@ -133,10 +133,34 @@ class Int8RotLinear(nn.Module):
         version = None if x.is_inference() else x._version
         hit = cache.get("x") is x and cache.get("version") == version and cache.get("group") == self.group
         quantized = cache["value"] if hit else kernels.rotate_quant(x2, self.group)
+        # a shared low-rank projection of the same input travels with the quantisation (see _lowrank_input)
+        self._lowrank_hit = cache.get("lowrank") if hit else None
         cache.clear()
         if self.keep_input:
             cache.update(x=x, version=version, group=self.group, value=quantized)
         return quantized
+
+    def _lowrank_input(self, x2: Tensor, kernels: SimpleNamespace) -> Tensor:
+        """``down(x)`` for the fused low-rank term.  Layers joined by ``share_lowrank`` that receive the same input
+        (q, k, v) compute ``x . [down_q; down_k; down_v]^T`` once and take their slice, extending the reference's
+        shared quantisation (int8.py:150-159) to the low-rank projection.  Call after ``_quantize``: the shared
+        result lives in the same cache and dies with it."""
+        peers = getattr(self, "_lowrank_peers", None)
+        stored, self._lowrank_hit = getattr(self, "_lowrank_hit", None), None
+        if not peers:
+            return kernels.lowrank_down(x2, self.down.weight)
+        if stored is not None and stored[0] is peers:
+            fused = stored[1]
+        else:
+            fused = kernels.lowrank_down(x2, torch.cat([layer.down.weight for layer in peers]))
+        if self.keep_input:
+            Int8RotLinear._last_input["lowrank"] = (peers, fused)
+        start = 0
+        for layer in peers:
+            if layer is self:
+                break
+            start += layer.rank
+        return fused[:, start:start + self.rank]
 
     def forward(self, x: Tensor) -> Tensor:
         shape = x.shape
@@ -147,8 +171,9 @@ class Int8RotLinear(nn.Module):
                 xq, sx = self._quantize(x, x2, kernels)
             else:
                 Int8RotLinear._last_input.clear()
+                self._lowrank_hit = None
                 xq, sx = kernels.rotate_quant_torch_rounding(x2, self.group)
-            xa = kernels.lowrank_down(x2, self.down.weight) if self.rank else None
+            xa = self._lowrank_input(x2, kernels) if self.rank else None
             y = kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
                                        up=self.up.weight if self.rank else None)
         else:
@@ -169,6 +194,19 @@ class Int8RotLinear(nn.Module):
         xq = torch.clamp(torch.round(xr / sx), -127, 127)
         acc = xq @ self.qweight.float().t()
         return (acc * sx * self.wscale[None, :]).to(torch.bfloat16)
+
+
+def share_lowrank(*layers: Int8RotLinear) -> None:
+    """Let layers that read one input (``to_q``, ``to_k``, ``to_v``) compute their low-rank ``down`` projections in
+    one pass over the input.  Sharing works together with ``keep_input`` (set it on all but the last layer), exactly
+    as the shared quantisation does; outputs are unchanged."""
+    if not layers or any(not isinstance(layer, Int8RotLinear) or not layer.rank for layer in layers):
+        raise ValueError("share_lowrank takes Int8RotLinear layers that have a low-rank term")
+    if len({layer.in_features for layer in layers}) != 1:
+        raise ValueError("layers sharing a low-rank projection must read the same input width")
+    peers = tuple(layers)
+    for layer in layers:
+        layer._lowrank_peers = peers
 
 
 # ------------------------------------------------------------------------------------------------- kernels
@@ -332,4 +370,5 @@ __all__ = [
     "regular_hadamard",
     "resolve_int8_gemm",
     "set_kernel_options",
+    "share_lowrank",
 ]

@@ -63,8 +63,9 @@ def head_to_seq(t: Tensor, group=None) -> Tensor:
 
 
 def attention_block_linears(x: Tensor, to_q, to_k, to_v, to_out, heads: int, attention=None, group=None) -> Tensor:
-    """One attention block's linears on this rank's tokens: q/k/v (sharing one quantisation when the layers have
-    ``keep_input``), the seq->head all-to-all, ``attention`` (identity -> v when None), head->seq, and ``to_out``."""
+    """One attention block's linears on this rank's tokens: q/k/v (sharing one quantisation -- and one low-rank
+    projection, see ``int8.share_lowrank`` -- when the layers have ``keep_input``), the seq->head all-to-all,
+    ``attention`` (identity -> v when None), head->seq, and ``to_out``."""
     q, k, v = to_q(x), to_k(x), to_v(x)
     qh, kh, vh = seq_to_head(q, heads, group), seq_to_head(k, heads, group), seq_to_head(v, heads, group)
     oh = vh if attention is None else attention(qh, kh, vh)

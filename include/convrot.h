@@ -133,6 +133,19 @@ void convrot_set_wait_limit_ns(uint64_t ns);
  */
 int convrot_set_gemm_mode(int mode);
 
+/*
+ * Kernel for group 256 in convrot_rotate_quant: 0 = automatic (the two-column team kernel for K <= 8192, else the
+ * one-column kernel used for the other groups), 1 = always one-column, 2 = always two-column.  All are bit-exact;
+ * the switch exists so tests cover each kernel.
+ */
+int convrot_set_rotate_variant(int variant);
+
+/*
+ * Launch shape of convrot_rotate_quant: row buffers per CTA (1..8) and CTAs per SM (1..32); 0 keeps the automatic
+ * choice.  Performance tuning only; results do not depend on it.
+ */
+int convrot_set_rotate_tuning(int stages, int ctas_per_sm);
+
 /* Library version (major * 10000 + minor * 100 + patch). */
 int convrot_version(void);
 

@@ -57,6 +57,14 @@ def _no_device_error():
     assert _lib.lib().convrot_poll_error(None) == 0
 
 
+@pytest.fixture(params=[2, 1], ids=["rot2col", "rot1col"])
+def rotate_variant(request):
+    """Group-256 rotation on the two-column team kernel and on the one-column kernel."""
+    _lib.check(_lib.lib().convrot_set_rotate_variant(request.param), "convrot_set_rotate_variant")
+    yield request.param
+    _lib.lib().convrot_set_rotate_variant(0)
+
+
 @pytest.fixture(params=[1, 2], ids=["gemm1sm", "gemm2sm"])
 def gemm_mode(request):
     """Runs a test on the 1-SM (128x256 tiles) and on the 2-SM (cta_group::2, 256x256 per CTA pair) kernel."""
@@ -72,7 +80,7 @@ def gemm_mode(request):
     (1, 256, 256), (17, 1024, 256), (70, 1024, 256), (333, 4096, 256), (64, 5120, 256), (40, 13824, 256),
     (33, 512, 16), (33, 1024, 64), (33, 64, 4), (5, 16384, 256), (3, 32768, 256), (129, 2048, 16),
 ])
-def test_rotate_quant_is_bitwise_the_oracle(M, K, group):
+def test_rotate_quant_is_bitwise_the_oracle(M, K, group, rotate_variant):
     x = edge_rows(synthetic.activations(M, K, seed=M + K), group)
     q, s = I.rotate_quant(x.to(DEV), group)
     q_ref, s_ref = O.rotate_quant(bits(x), group)
@@ -81,7 +89,7 @@ def test_rotate_quant_is_bitwise_the_oracle(M, K, group):
 
 
 @pytest.mark.parametrize("group", [16, 64, 256])
-def test_rotate_quant_is_bitwise_the_reference_kernel(group):
+def test_rotate_quant_is_bitwise_the_reference_kernel(group, rotate_variant):
     t = np.load(os.path.join(GOLDEN, "triton_kernels.npz"))
     q, s = I.rotate_quant(from_bits(t["x"]).to(DEV), group)
     assert np.array_equal(q.cpu().numpy(), t[f"dense_exact_g{group}_q"])
@@ -93,7 +101,7 @@ def test_rotate_quant_is_bitwise_the_reference_kernel(group):
 
 
 @pytest.mark.parametrize("M,K,group", [(8, 1024, 256), (16, 512, 16), (3, 256, 64), (1, 5120, 256)])
-def test_torch_rounding_mode_is_bitwise_the_reference_cpu_path(M, K, group):
+def test_torch_rounding_mode_is_bitwise_the_reference_cpu_path(M, K, group, rotate_variant):
     x = synthetic.activations(M, K, seed=11)
     q, s = I.rotate_quant_torch_rounding(x.to(DEV), group)
     q_ref, s_ref = O.rotate_quant_cpu(bits(x), group)
@@ -291,3 +299,29 @@ def test_one_and_two_sm_kernels_agree_bitwise(M, N, K, r):
     # the low-rank MMA accumulates 256 vs 128 rows per instruction: allow the fp32 accumulation order to differ
     a, b = outs[0][0].float(), outs[1][0].float()
     assert ((a - b).abs() <= a.abs() * 2.0**-7 + 1e-2 * a.abs().max()).all()
+
+
+def test_shared_lowrank_projection_matches_separate_layers(monkeypatch):
+    """q/k/v with share_lowrank run one down projection over x and give the same outputs as separate layers."""
+    kernels = I._kernels()
+    calls = []
+    down = kernels.lowrank_down
+    monkeypatch.setattr(kernels, "lowrank_down", lambda *a: calls.append(a[1].shape[0]) or down(*a))
+
+    def layer(seed):
+        w = synthetic.linear_weights(1024, 512, rank=32, bias=True, group=256, seed_offset=seed)
+        m = I.Int8RotLinear(1024, 512, 256, bias=True, rank=32)
+        synthetic.load_into(m, w)
+        return m.to(DEV)
+
+    to_q, to_k, to_v = layer(0), layer(1), layer(2)
+    x = synthetic.activations(300, 1024).to(DEV)
+    separate = [to_q(x), to_k(x), to_v(x)]
+    assert calls == [32, 32, 32]
+    calls.clear()
+    I.share_lowrank(to_q, to_k, to_v)
+    to_q.keep_input = to_k.keep_input = True
+    shared = [to_q(x), to_k(x), to_v(x)]
+    assert calls == [96] and not I.Int8RotLinear._last_input
+    for a, b in zip(separate, shared, strict=True):
+        assert torch.equal(a, b)
