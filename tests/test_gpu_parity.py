@@ -325,3 +325,36 @@ def test_shared_lowrank_projection_matches_separate_layers(monkeypatch):
     assert calls == [96] and not I.Int8RotLinear._last_input
     for a, b in zip(separate, shared, strict=True):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M,K,N,r", [(333, 5120, 5120, 32), (17, 1024, 300, 0), (1024, 4096, 2048, 64)])
+def test_convrot_linear_with_a_workspace_matches_the_module(M, K, N, r):
+    """convrot_linear (C ABI: rotate+quantise into a caller workspace, then the GEMM) equals the module's calls."""
+    import ctypes
+
+    L = _lib.lib()
+    x = synthetic.activations(M, K, seed=41).to(DEV)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256).to(DEV)
+    nbytes = L.convrot_workspace_size(M, K, r)
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=DEV)
+    base = (ws.data_ptr() + 255) // 256 * 256
+    ldy = -(-N // 8) * 8  # bf16 leading dimensions are multiples of 8 (16 bytes)
+    y_full = torch.empty(M, ldy, dtype=torch.bfloat16, device=DEV)
+    P = ctypes.c_void_p
+    rc = L.convrot_linear(P(x.data_ptr()), K, P(w.qweight.data_ptr()), K, P(w.wscale.data_ptr()),
+                          P(w.bias.data_ptr()), P(w.down.data_ptr()) if r else None, K,
+                          P(w.up.data_ptr()) if r else None, r, r, M, N, K, 256, P(base), nbytes,
+                          P(y_full.data_ptr()), ldy, P(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "convrot_linear")
+    y = y_full[:, :N]
+    # an odd leading dimension is refused, not written through
+    assert L.convrot_linear(P(x.data_ptr()), K, P(w.qweight.data_ptr()), K, P(w.wscale.data_ptr()), None, None, 0,
+                            None, 0, 0, M, N, K, 256, P(base), nbytes, P(y_full.data_ptr()), ldy + 1,
+                            None) == (_lib.ERR_ALIGN if (ldy + 1) % 8 else _lib.OK)
+    layer = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+    synthetic.load_into(layer, w.to("cpu"))
+    ref = layer.to(DEV)(x)
+    if M >= I._MIN_KERNEL_ROWS:
+        assert torch.equal(y, ref)
+    else:  # the module reproduces the reference's torch-path rounding below 17 rows; the C entry does not
+        assert close(y.float().cpu().numpy(), ref.float().cpu().numpy())[1] >= 0.9999
