@@ -13,7 +13,8 @@ import os
 from .build import LIB
 
 # Status codes (include/convrot.h).
-OK, ERR_SHAPE, ERR_GROUP, ERR_ALIGN, ERR_CUDA, ERR_ARCH, ERR_TIMEOUT, ERR_ARG = range(8)
+OK, ERR_SHAPE, ERR_GROUP, ERR_ALIGN, ERR_CUDA, ERR_ARCH, ERR_TIMEOUT, ERR_ARG, ERR_SCRATCH = range(9)
+NOALLOC_SCRATCH_BYTES = 16 << 20
 ROUND_KERNEL, ROUND_TORCH = 0, 1
 
 _P, _I, _L, _S, _U64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
@@ -26,6 +27,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_gemm_acc": ([_P, _L, _P, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_workspace_size": ([_L, _L, _L], _S),
     "convrot_linear": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _S, _P, _L, _P], _I),
+    "convrot_linear_noalloc": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _L, _P], _I),
     "convrot_status_string": ([_I], ctypes.c_char_p),
     "convrot_last_cuda_error": ([], _I),
     "convrot_poll_error": ([_P], _I),
@@ -63,7 +65,7 @@ def check(code: int, what: str) -> None:
     if code == OK:
         return
     message = f"{what}: {status_string(code)}"
-    if code in (ERR_SHAPE, ERR_GROUP, ERR_ALIGN, ERR_ARG):
+    if code in (ERR_SHAPE, ERR_GROUP, ERR_ALIGN, ERR_ARG, ERR_SCRATCH):
         raise ValueError(message)
     if code == ERR_CUDA:
         message += f" (CUDA error {lib().convrot_last_cuda_error()})"

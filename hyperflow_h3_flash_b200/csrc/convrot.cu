@@ -21,6 +21,12 @@ namespace convrot {
 
 __device__ int g_error_word;  // CONVROT_ERR_TIMEOUT after a bounded wait expired; cleared by convrot_poll_error
 
+// Scratch of convrot_linear_noalloc: the codes, scales and low-rank input of one call live here instead of in a
+// caller allocation.  It is part of the library's device image, so every GPU that loads the library holds these
+// CONVROT_NOALLOC_SCRATCH_BYTES until the process exits.  In host code the name is only a host-side stand-in:
+// its device address comes from cudaGetSymbolAddress (see noalloc_scratch below), never from the name itself.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CONVROT_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local int t_last_cuda_error = 0;
@@ -34,6 +40,7 @@ struct DeviceState {
   int status = CONVROT_OK;
   int sms = 0;
   int* error_word = nullptr;
+  uint8_t* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device (first no-alloc call)
 };
 
 constexpr int kMaxDevices = 64;
@@ -439,6 +446,32 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
 
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
+// Bytes convrot_linear needs for q (int8 [M, ldq]), s (fp32 [M]) and xa (bf16 [M, ldxa]), each 256-byte aligned.
+size_t linear_workspace_need(int64_t M, int64_t K, int64_t r) {
+  const int64_t ldxa = (r + 7) / 8 * 8;
+  const int64_t ldq = (K + 15) / 16 * 16;
+  return align256(static_cast<size_t>(M) * ldq) + align256(static_cast<size_t>(M) * 4) +
+         align256(static_cast<size_t>(M) * ldxa * 2);
+}
+
+// Device address of the no-alloc scratch on the current device, looked up once per device (with that device
+// current) and kept in the device state.  cudaGetSymbolAddress allocates nothing.
+int noalloc_scratch(uint8_t** out) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (!st->noalloc_scratch) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (!ptr || (reinterpret_cast<uintptr_t>(ptr) & 255u)) return CONVROT_ERR_CUDA;
+    st->noalloc_scratch = static_cast<uint8_t*>(ptr);
+  }
+  *out = st->noalloc_scratch;
+  return CONVROT_OK;
+}
+
 }  // namespace
 }  // namespace convrot
 
@@ -490,8 +523,7 @@ int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, con
   const int64_t rr = has_lr ? r : 0;
   const int64_t ldxa = (rr + 7) / 8 * 8;
   const int64_t ldq = (K + 15) / 16 * 16;
-  const size_t need = align256(static_cast<size_t>(M) * ldq) + align256(static_cast<size_t>(M) * 4) +
-                      align256(static_cast<size_t>(M) * ldxa * 2);
+  const size_t need = linear_workspace_need(M, K, rr);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return CONVROT_ERR_ARG;
   uint8_t* ws_bytes = static_cast<uint8_t*>(workspace);
   int8_t* q = reinterpret_cast<int8_t*>(ws_bytes);
@@ -504,6 +536,23 @@ int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, con
                       M, N, K, y, ldy, stream);
 }
 
+int convrot_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* ws,
+                           const void* bias, const void* lr_down, int64_t ld_down, const void* lr_up, int64_t ld_up,
+                           int64_t r, int64_t M, int64_t N, int64_t K, int group, void* y, int64_t ldy,
+                           void* stream) {
+  if (M < 0 || K <= 0 || r < 0) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  const bool has_lr = lr_down && lr_up && r > 0;
+  if (linear_workspace_need(M, K, has_lr ? r : 0) > CONVROT_NOALLOC_SCRATCH_BYTES) return CONVROT_ERR_SCRATCH;
+  uint8_t* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // The same two launches as convrot_linear, with the built-in scratch as the workspace.  Both kernels write their
+  // part of the scratch completely before anything reads it, so no part needs clearing between calls.
+  return convrot_linear(x, ldx, w, ldw, ws, bias, lr_down, ld_down, lr_up, ld_up, r, M, N, K, group, scratch,
+                        CONVROT_NOALLOC_SCRATCH_BYTES, y, ldy, stream);
+}
+
 const char* convrot_status_string(int status) {
   switch (status) {
     case CONVROT_OK: return "ok";
@@ -514,6 +563,7 @@ const char* convrot_status_string(int status) {
     case CONVROT_ERR_ARCH: return "device is not sm_100 (B200)";
     case CONVROT_ERR_TIMEOUT: return "a kernel's bounded wait expired";
     case CONVROT_ERR_ARG: return "missing pointer or unknown option";
+    case CONVROT_ERR_SCRATCH: return "problem needs more than the built-in scratch of convrot_linear_noalloc";
     default: return "unknown status";
   }
 }

@@ -45,6 +45,7 @@ extern "C" {
 #define CONVROT_ERR_ARCH 5        /* the current device is not sm_100 (B200 / GB200) */
 #define CONVROT_ERR_TIMEOUT 6     /* a kernel's bounded wait expired (see convrot_poll_error) */
 #define CONVROT_ERR_ARG 7         /* a required pointer is NULL or an option is unknown */
+#define CONVROT_ERR_SCRATCH 8     /* convrot_linear_noalloc: the problem needs more than its built-in scratch */
 
 /* Rotation arithmetic of convrot_rotate_quant. */
 #define CONVROT_ROUND_KERNEL 0 /* reference CUDA path (int8.py:194-221): exact dot rounded once to fp32,
@@ -109,6 +110,35 @@ int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, con
                    const void* lr_down, int64_t ld_down, const void* lr_up, int64_t ld_up, int64_t r,
                    int64_t M, int64_t N, int64_t K, int group, void* workspace, size_t workspace_bytes,
                    void* y, int64_t ldy, void* stream);
+
+/*
+ * The whole layer without any allocation (no counterpart in the reference): the same computation as
+ * convrot_linear, with the workspace replaced by scratch built into the library.
+ *
+ * For callers that cannot allocate device memory on the call path: hosts that own all device memory and forbid
+ * allocations once serving has started (a fixed arena planned at start-up), plugin-style interfaces whose enqueue
+ * call hands over only the inputs, the outputs and a stream, and code that must not call cudaMalloc / cudaFree
+ * because those can synchronise the device and stall every other stream.  This function calls no cudaMalloc,
+ * cudaFree or allocating library routine.
+ *
+ * Limit: the codes, scales and low-rank input of one call must fit CONVROT_NOALLOC_SCRATCH_BYTES (16 MiB), i.e.
+ * convrot_workspace_size(M, K, r) rounded as convrot_linear rounds it (for example M = 3072 rows at K = 5120);
+ * larger problems return CONVROT_ERR_SCRATCH without launching anything.  The scratch is part of the library's
+ * device image: every GPU that loads the library holds those 16 MiB until the process exits.
+ *
+ * Set-up: the first call on a device (with that device current) looks up the scratch's device address once;
+ * make that first call before any stream capture.
+ *
+ * Sharing: all calls, on all streams, use the same scratch and it keeps the last call's contents.  Nothing in it
+ * has to start at zero (each call writes its codes, scales and low-rank input before reading them), but calls
+ * whose work overlaps on the GPU race on the scratch: order them on one stream, or otherwise make one finish
+ * before the next starts.
+ */
+#define CONVROT_NOALLOC_SCRATCH_BYTES (16u << 20)
+int convrot_linear_noalloc(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* ws,
+                           const void* bias, const void* lr_down, int64_t ld_down, const void* lr_up, int64_t ld_up,
+                           int64_t r, int64_t M, int64_t N, int64_t K, int group, void* y, int64_t ldy,
+                           void* stream);
 
 /* Name of a status code. */
 const char* convrot_status_string(int status);
