@@ -171,7 +171,7 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
 
 template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
 int launch_gemm2(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
-                 const CUtensorMap& tup, const GemmParams& p, cudaStream_t stream) {
+                 const CUtensorMap& tup, const CUtensorMap& ty, const GemmParams& p, cudaStream_t stream) {
   auto kernel = convrot_gemm2sm_kernel<Cfg, EPI, LR_ATOM, LR_ATOMS>;
   const int pair_tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
   int clusters = -1;
@@ -192,7 +192,7 @@ int launch_gemm2(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap
     store_resident(reinterpret_cast<const void*>(kernel), clusters);
   }
   const int pairs = pair_tiles < clusters ? pair_tiles : clusters;
-  kernel<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
+  kernel<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, ty, p);
   e = cudaGetLastError();
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
@@ -203,9 +203,9 @@ using CfgI8 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 0, 0>;
 using CfgI8LR32 = GemmCfg<KIND_I8, 256, 4, EPI_DEQUANT, 64, 1>;
 using CfgI8LR64 = GemmCfg<KIND_I8, 256, 3, EPI_DEQUANT, 128, 1>;
 using CfgRaw = GemmCfg<KIND_I8, 256, 4, EPI_RAW_I32, 0, 0>;
-using Cfg2 = Gemm2Cfg<6, 0, 0>;
-using Cfg2LR32 = Gemm2Cfg<6, 64, 1>;
-using Cfg2LR64 = Gemm2Cfg<6, 128, 1>;
+using Cfg2 = Gemm2Cfg<5, 0, 0>;
+using Cfg2LR32 = Gemm2Cfg<5, 64, 1>;
+using Cfg2LR64 = Gemm2Cfg<5, 128, 1>;
 
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
@@ -254,10 +254,13 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   if (two_sm) {
-    if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, p, stream);
-    if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, p, stream);
-    if (lr_atom == 64) return launch_gemm2<Cfg2LR32, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, p, stream);
-    return launch_gemm2<Cfg2LR64, EPI_DEQUANT, 128, 1>(*st, ta, tb, txa, tup, p, stream);
+    CUtensorMap ty;  // bf16 output, 32 x 32 boxes for the epilogue's TMA stores
+    memset(&ty, 0, sizeof(ty));
+    if (!raw && (rc = make_map(&ty, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldo, 32, 32))) return rc;
+    if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
+    if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
+    if (lr_atom == 64) return launch_gemm2<Cfg2LR32, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, ty, p, stream);
+    return launch_gemm2<Cfg2LR64, EPI_DEQUANT, 128, 1>(*st, ta, tb, txa, tup, ty, p, stream);
   }
   if (raw) return launch_gemm<CfgRaw, KIND_I8, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, p, stream);
   if (!has_lr) return launch_gemm<CfgI8, KIND_I8, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, p, stream);

@@ -137,7 +137,11 @@ struct Gemm2Cfg {
   // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2], lr_done[2], lr_full, lr_empty, drain
   static constexpr int kNumBars = 2 * STAGES + 8 + 3;
   static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
-  static constexpr int kSmemBytes = 1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kBarBytes;
+  // Output staging: per epilogue warp two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B) for TMA stores.
+  static constexpr int kStoreBoxBytes = 32 * 64;
+  static constexpr int kStoreBytes = 4 * 2 * kStoreBoxBytes;
+  static constexpr int kSmemBytes =
+      1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kStoreBytes + kBarBytes;
   static constexpr uint32_t kIdesc = make_idesc_i8(256, 256);
   static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 256);
 };
@@ -146,7 +150,7 @@ template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     convrot_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_xa, const __grid_constant__ CUtensorMap tmap_up,
-                           const GemmParams p) {
+                           const __grid_constant__ CUtensorMap tmap_y, const GemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int S = Cfg::kStages;
   constexpr bool HAS_LR = Cfg::kHasLR;
@@ -155,7 +159,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   uint8_t* ring = smem;
   uint8_t* lr_xa = ring + S * Cfg::kStageBytes;
   uint8_t* lr_up = lr_xa + Cfg::kLRXaBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(lr_up + Cfg::kLRUpBytes);
+  uint8_t* store_stage = lr_up + Cfg::kLRUpBytes;  // 1024-aligned: stage and tile sizes are multiples of 1 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(store_stage + Cfg::kStoreBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tmem_full = bars + 2 * S;
@@ -383,6 +388,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     // ------------------------------------------------------------ epilogue over this CTA's 128 rows
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
+    // bf16 results leave through shared memory and TMA stores: each lane writes its row's 64 bytes of a 32 x 32
+    // box (SWIZZLE_64B: 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3), so a quarter-warp hits all
+    // banks), then lane 0 stores the box; two boxes per warp alternate.
+    uint8_t* my_boxes = store_stage + (warp - 2) * 2 * Cfg::kStoreBoxBytes;
+    int box_sel = 0;
+    auto stage_and_store = [&](const float (&t)[32], int m_box, int n_col) {
+      uint8_t* box = my_boxes + box_sel * Cfg::kStoreBoxBytes;
+      if (lane == 0) bulk_wait_group_read<1>();  // the store that used this box two chunks ago has read it
+      __syncwarp();
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int pc = c ^ ((lane >> 1) & 3);
+        *reinterpret_cast<uint4*>(box + lane * 64 + pc * 16) =
+            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&tmap_y, box, n_col, m_box);
+        bulk_commit_group();
+      }
+      box_sel ^= 1;
+    };
     int i = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
       const uint32_t buf = i & 1;
@@ -412,9 +446,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
-          } else if (row_ok) {
-            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n, t,
-                             n, p.N);
+          } else {
+            stage_and_store(t, m0 + quad * 32, n);  // rows beyond M are clipped by the TMA store
           }
         }
         if (HAS_LR) {
@@ -432,12 +465,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             uint32_t v[32];
             tmem_ld_32x32b_x32(taddr + c, v);
             tmem_ld_wait();
-            if (!row_ok) continue;
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n0 + c,
-                             t, n0 + c, p.N);
+            stage_and_store(t, m0 + quad * 32, n0 + c);
           }
         }
       } else {  // EPI_RAW_I32
@@ -464,6 +495,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(leader_tmem_empty0 + buf * 8);
     }
+    if (lane == 0) bulk_wait_group_all();  // every output store has landed before the CTA leaves
+    __syncwarp();
   }
 
   tc_fence_before();
