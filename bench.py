@@ -244,6 +244,8 @@ class KernelTimer:
         self._wrap("rotate_quant", "rq", 1)
         self._wrap("rotate_quant_torch_rounding", "rq", 1)
         self._wrap("lowrank_down", "down", 1)
+        self._wrap("rotate_quant_packed", "rq", 1)
+        self._wrap("lowrank_down_packed", "down", 1)
         return self
 
     def __exit__(self, *exc):

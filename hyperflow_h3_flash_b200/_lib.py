@@ -25,6 +25,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_lowrank_down": ([_P, _L, _P, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_gemm": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_gemm_acc": ([_P, _L, _P, _L, _L, _L, _L, _P, _L, _P], _I),
+    "convrot_gemm_packed": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
+    "convrot_rotate_quant_packed": ([_P, _L, _L, _L, _I, _I, _P, _L, _P, _P], _I),
+    "convrot_lowrank_down_packed": ([_P, _L, _P, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_workspace_size": ([_L, _L, _L], _S),
     "convrot_linear": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _S, _P, _L, _P], _I),
     "convrot_linear_noalloc": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _L, _P], _I),

@@ -13,8 +13,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "libconvrot.so")
-SOURCES = [os.path.join(HERE, "csrc", name) for name in ("convrot.cu", "gemm_sm100.cuh", "rotate_quant.cuh",
-                                                          "ptx.cuh")]
+SOURCES = sorted(os.path.join(HERE, "csrc", name) for name in os.listdir(os.path.join(HERE, "csrc"))
+                 if name.endswith((".cu", ".cuh", ".h")))
 HEADER = os.path.join(os.path.dirname(HERE), "include", "convrot.h")
 
 NVCC_FLAGS = [

@@ -146,6 +146,29 @@ void store_resident(const void* fn, int resident) {
   if (g_launch_cache_n < kLaunchCacheSize) g_launch_cache[g_launch_cache_n++] = {fn, dev, resident};
 }
 
+// 3-D map over "chunked rows": element (m, k) at base + (k / W) * S + m * L + k % W, i.e. dims (W, M, K / W) with
+// byte strides (L * elem, S * elem); box box_cols x box_rows x 1, swizzle as make_map.
+int make_map3(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem, int64_t rows, int64_t W,
+              int64_t chunks, int64_t L, int64_t S, int box_rows, int box_cols) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(chunks)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(L * elem),
+                           static_cast<cuuint64_t>((chunks > 1 ? S : L * rows) * elem)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const int inner = box_cols * elem;
+  CUtensorMapSwizzle sw = inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : inner == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                        : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return CONVROT_ERR_CUDA;
+  }
+  return CONVROT_OK;
+}
+
 template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
 int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
                 const CUtensorMap& tup, const GemmParams& p, cudaStream_t stream) {
@@ -207,9 +230,14 @@ using Cfg2 = Gemm2Cfg<5, 0, 0>;
 using Cfg2LR32 = Gemm2Cfg<5, 64, 1>;
 using Cfg2LR64 = Gemm2Cfg<5, 128, 1>;
 
+// out_chunk > 0 writes the bf16 output as [N / out_chunk, M, out_chunk] (the Ulysses send layout) and ignores ldo.
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
-            int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream) {
+            int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream, int64_t out_chunk = 0) {
+  if (out_chunk > 0) {
+    if (raw || out_chunk % 32 || N % out_chunk) return CONVROT_ERR_SHAPE;
+    ldo = out_chunk;
+  }
   if (M < 0 || N <= 0 || K <= 0) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || N > (1 << 24)) return CONVROT_ERR_SHAPE;
@@ -218,7 +246,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   const bool has_lr = !raw && xa && up && r > 0;
   if (!raw && (xa || up) && !has_lr) return CONVROT_ERR_ARG;
   if (has_lr && r > 64) return CONVROT_ERR_SHAPE;
-  if (K % 16 || ldq < K || ldw < K || ldo < N) return CONVROT_ERR_SHAPE;
+  if (K % 16 || ldq < K || ldw < K || ldo < (out_chunk > 0 ? out_chunk : N)) return CONVROT_ERR_SHAPE;
   if (ldq % 16 || ldw % 16 || !aligned16(q) || !aligned16(w)) return CONVROT_ERR_ALIGN;
   if (raw ? (ldo % 4 || !aligned16(out)) : (ldo % 8 || !aligned16(out))) return CONVROT_ERR_ALIGN;
   if (!raw && (!aligned16(ws) || (bias && !aligned16(bias)))) return CONVROT_ERR_ALIGN;
@@ -234,7 +262,12 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   CUtensorMap ta, tb, txa, tup;
   memset(&txa, 0, sizeof(txa));
   memset(&tup, 0, sizeof(tup));
-  if ((rc = make_map(&ta, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, ldq, kBM, 128))) return rc;
+  // A: 2-D for the 2-SM kernel, a one-chunk 3-D map for the 1-SM kernel (which also serves chunked bf16 inputs)
+  if (two_sm) {
+    if ((rc = make_map(&ta, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, ldq, kBM, 128))) return rc;
+  } else if ((rc = make_map3(&ta, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, M, K, 1, ldq, 0, kBM, 128))) {
+    return rc;
+  }
   if ((rc = make_map(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldw, b_rows, 128))) return rc;
   const int lr_atom = r <= 32 ? 64 : 128;
   if (has_lr) {
@@ -250,13 +283,18 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.out = out;
   p.ldo = ldo;
+  p.out_chunk = out_chunk > 0 ? static_cast<int>(out_chunk) : static_cast<int>(N);
+  p.out_chunk_stride = out_chunk > 0 ? M * out_chunk : 0;
+  p.a_chunk = static_cast<int>(K);
   p.r = has_lr ? static_cast<int>(r) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   if (two_sm) {
     CUtensorMap ty;  // bf16 output, 32 x 32 boxes for the epilogue's TMA stores
     memset(&ty, 0, sizeof(ty));
-    if (!raw && (rc = make_map(&ty, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, N, ldo, 32, 32))) return rc;
+    if (!raw && (rc = make_map3(&ty, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, p.out_chunk, N / p.out_chunk,
+                                ldo, p.out_chunk_stride, 32, 32)))
+      return rc;
     if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
     if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
     if (lr_atom == 64) return launch_gemm2<Cfg2LR32, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, ty, p, stream);
@@ -272,13 +310,16 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
 template <int BN, int STAGES>
 using CfgDown = GemmCfg<KIND_BF16, BN, STAGES, EPI_BF16, 0, 0>;
 
+// x in chunked rows (W = x_chunk, S = x_chunk_stride; plain rows: x_chunk = K).
 int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, int64_t M, int64_t K, int64_t r,
-                 void* xa, int64_t ldxa, cudaStream_t stream) {
+                 void* xa, int64_t ldxa, cudaStream_t stream, int64_t x_chunk = 0, int64_t x_chunk_stride = 0) {
+  if (x_chunk <= 0) x_chunk = K;
+  if (K % x_chunk || (x_chunk != K && (x_chunk % 64 || x_chunk_stride % 8))) return CONVROT_ERR_SHAPE;
   if (M < 0 || K <= 0 || r <= 0) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
   if (M > INT32_MAX || K > INT32_MAX || r > 256) return CONVROT_ERR_SHAPE;
   if (!x || !down || !xa) return CONVROT_ERR_ARG;
-  if (K % 8 || ldx < K || ld_down < K || ldxa < r) return CONVROT_ERR_SHAPE;
+  if (K % 8 || ldx < x_chunk || ld_down < K || ldxa < r) return CONVROT_ERR_SHAPE;
   if (ldx % 8 || ld_down % 8 || ldxa % 8 || !aligned16(x) || !aligned16(down) || !aligned16(xa))
     return CONVROT_ERR_ALIGN;
   DeviceState* st = nullptr;
@@ -287,7 +328,9 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
   const int bn = r <= 32 ? 32 : r <= 64 ? 64 : r <= 128 ? 128 : 256;
   CUtensorMap ta, tb, tz;
   memset(&tz, 0, sizeof(tz));
-  if ((rc = make_map(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, ldx, kBM, 64))) return rc;
+  if ((rc = make_map3(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, x_chunk, K / x_chunk, ldx, x_chunk_stride,
+                      kBM, 64)))
+    return rc;
   if ((rc = make_map(&tb, down, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, r, K, ld_down, bn, 64))) return rc;
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -296,6 +339,9 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
   p.K = static_cast<int>(K);
   p.out = xa;
   p.ldo = ldxa;
+  p.out_chunk = static_cast<int>(r);
+  p.out_chunk_stride = 0;
+  p.a_chunk = static_cast<int>(x_chunk);
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   switch (bn) {
@@ -368,16 +414,40 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   int threads = (ngroups * 8 + slots - 1) / slots;
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
+  const bool chunked = p.x_chunk != p.K;
+  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
+  void (*kernel)(const RotQuantParams) = nullptr;
+  if (slots == 1 && !chunked)
+    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, false> : rotate_quant256_kernel<1, 0, false>;
+  else if (slots == 1)
+    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, true> : rotate_quant256_kernel<1, 0, true>;
+  else if (!chunked)
+    kernel = torch_rounding ? rotate_quant256_kernel<2, 1, false> : rotate_quant256_kernel<2, 0, false>;
+  else
+    kernel = torch_rounding ? rotate_quant256_kernel<2, 1, true> : rotate_quant256_kernel<2, 0, true>;
+  int regs = -1;  // the kernel's registers per thread, cached with the shared-memory opt-in
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &regs);
+  if (rc) return rc;
+  cudaError_t e;
+  if (regs < 0) {
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
+      return cuda_fail(e);
+    cudaFuncAttributes attr;
+    if ((e = cudaFuncGetAttributes(&attr, kernel)) != cudaSuccess) return cuda_fail(e);
+    regs = attr.numRegs > 0 ? attr.numRegs : 128;
+    store_resident(reinterpret_cast<const void*>(kernel), regs);
+  }
   // The per-row work is a serial chain (exact rotation, block-wide amax, quantise), so throughput comes from
-  // resident CTAs: fill the SM with as many CTAs as registers allow (~96 per thread), then give each the deepest
-  // row ring that still fits (measured on B200: K = 5120 -> 4 CTAs x 3 row buffers).
-  const int regs_per_thread = slots == 1 ? 96 : 128;
-  int best_blocks = 65536 / (threads * regs_per_thread);
+  // resident CTAs: fill the SM with as many CTAs as its registers hold (allocated per warp in units of 8 per
+  // thread), then give each the deepest row ring that still fits (measured on B200: K = 5120 -> 4 CTAs x 3 row
+  // buffers).
+  const int regs_alloc = (regs + 7) / 8 * 8;
+  int best_blocks = 65536 / (threads * regs_alloc);
   if (best_blocks > 2048 / threads) best_blocks = 2048 / threads;
   if (best_blocks < 1) best_blocks = 1;
   int best_stages = 1;
   for (int stages = 2; stages <= kRQMaxStages; ++stages) {
-    const size_t sm = rq256_smem_bytes(p.K, threads, stages);
+    const size_t sm = rq256_smem_bytes(p.K, threads, stages, chunked);
     if (sm > 227 * 1024 || static_cast<size_t>(best_blocks) * (sm + 1024) > 228 * 1024) break;
     best_stages = stages;
   }
@@ -385,23 +455,8 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   q.stages = best_stages;
   if (g_rq_stages > 0) q.stages = g_rq_stages;
   if (g_rq_blocks > 0) best_blocks = g_rq_blocks;
-  const size_t smem = rq256_smem_bytes(p.K, threads, q.stages);
+  const size_t smem = rq256_smem_bytes(p.K, threads, q.stages, chunked);
   if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
-  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
-  void (*kernel)(const RotQuantParams) = nullptr;
-  if (slots == 1)
-    kernel = torch_rounding ? rotate_quant256_kernel<1, 1> : rotate_quant256_kernel<1, 0>;
-  else
-    kernel = torch_rounding ? rotate_quant256_kernel<2, 1> : rotate_quant256_kernel<2, 0>;
-  int opted = -1;
-  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &opted);
-  if (rc) return rc;
-  cudaError_t e;
-  if (opted < 0) {
-    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
-      return cuda_fail(e);
-    store_resident(reinterpret_cast<const void*>(kernel), 1);
-  }
   int64_t grid = static_cast<int64_t>(st.sms) * best_blocks;
   if (grid > p.M) grid = p.M;
   kernel<<<static_cast<int>(grid), threads, smem, stream>>>(q);
@@ -410,11 +465,14 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
 }
 
 int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding, int8_t* q, int64_t ldq,
-                 float* s, cudaStream_t stream) {
+                 float* s, cudaStream_t stream, int64_t x_chunk = 0, int64_t x_chunk_stride = 0) {
+  if (x_chunk <= 0) x_chunk = K;
+  if (x_chunk != K && (K % x_chunk || x_chunk % 128 || x_chunk_stride % 8 || x_chunk > INT32_MAX))
+    return CONVROT_ERR_SHAPE;
   if (M < 0 || K <= 0) return CONVROT_ERR_SHAPE;
   if (group != 4 && group != 16 && group != 64 && group != 256) return CONVROT_ERR_GROUP;
   if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
-  if (K % group || K % 16 || K > 32768 || ldx < K || ldq < K || M > INT32_MAX) return CONVROT_ERR_SHAPE;
+  if (K % group || K % 16 || K > 32768 || ldx < x_chunk || ldq < K || M > INT32_MAX) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
   if (!x || !q || !s) return CONVROT_ERR_ARG;
   if (ldx % 8 || ldq % 16 || !aligned16(x) || !aligned16(q)) return CONVROT_ERR_ALIGN;
@@ -424,6 +482,8 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
   RotQuantParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);
   p.ldx = ldx;
+  p.x_chunk = static_cast<int>(x_chunk);
+  p.x_chunk_stride = x_chunk_stride;
   p.M = static_cast<int>(M);
   p.K = static_cast<int>(K);
   p.q = q;
@@ -489,6 +549,28 @@ int convrot_rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int g
   int rc = rotate_quant(x, ldx, M, K, group, rounding, q_out, ldq, s_out, s);
   if (rc || !lr_down) return rc;
   return lowrank_down(x, ldx, lr_down, ld_down, M, K, r, xa_out, ldxa, s);
+}
+
+int convrot_rotate_quant_packed(const void* x, int64_t chunk_cols, int64_t M, int64_t K, int group, int rounding,
+                                int8_t* q_out, int64_t ldq, float* s_out, void* stream) {
+  if (chunk_cols <= 0 || M < 0) return CONVROT_ERR_SHAPE;
+  return rotate_quant(x, chunk_cols, M, K, group, rounding, q_out, ldq, s_out, static_cast<cudaStream_t>(stream),
+                      chunk_cols, M * chunk_cols);
+}
+
+int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* lr_down, int64_t ld_down, int64_t M,
+                                int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream) {
+  if (chunk_cols <= 0 || M < 0) return CONVROT_ERR_SHAPE;
+  return lowrank_down(x, chunk_cols, lr_down, ld_down, M, K, r, xa_out, ldxa, static_cast<cudaStream_t>(stream),
+                      chunk_cols, M * chunk_cols);
+}
+
+int convrot_gemm_packed(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                        const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                        int64_t M, int64_t N, int64_t K, void* y, int64_t chunk_cols, void* stream) {
+  if (chunk_cols <= 0) return CONVROT_ERR_SHAPE;
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, chunk_cols, false,
+                 static_cast<cudaStream_t>(stream), chunk_cols);
 }
 
 int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down, int64_t M, int64_t K,

@@ -33,17 +33,31 @@ namespace convrot {
 enum { KIND_I8 = 0, KIND_BF16 = 1 };
 enum { EPI_DEQUANT = 0, EPI_RAW_I32 = 1, EPI_BF16 = 2 };
 
+// Operand / output layout "chunked rows": element (m, k) at base + (k / W) * S + m * L + k % W.  Plain row-major
+// storage is the one-chunk case W = K (L = leading dimension); the Ulysses all-to-all buffers are W = K / P,
+// L = W, S = M * W (all tokens of head block j, then block j + 1, ...).
 struct GemmParams {
   int M, N, K;
   const float* sa;      // [M]   (EPI_DEQUANT)
   const float* sb;      // [N]   (EPI_DEQUANT)
   const __nv_bfloat16* bias;  // [N] or null
   void* out;            // bf16 [M, N] or int32 [M, N]
-  int64_t ldo;          // elements
+  int64_t ldo;          // elements (row pitch L of the output)
+  int out_chunk;        // W of the output (N for plain rows)
+  int64_t out_chunk_stride;  // S of the output (elements)
+  int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
   uint64_t wait_limit_ns;
   int* error_word;
 };
+
+// Pointer to output column n (a multiple of 32 inside one chunk) of row `row`.
+template <class T>
+__device__ __forceinline__ T* out_ptr(const GemmParams& p, int row, int n) {
+  const int j = n / p.out_chunk;
+  return reinterpret_cast<T*>(p.out) + j * p.out_chunk_stride + static_cast<int64_t>(row) * p.ldo +
+         (n - j * p.out_chunk);
+}
 
 constexpr int kBM = 128;
 constexpr int kRowBytes = 128;  // bytes of K per stage row (one SWIZZLE_128B atom)
@@ -233,7 +247,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           }
           uint8_t* sa_ptr = ring + stage * Cfg::kStageBytes;
           mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-          tma_load_2d(sa_ptr, &tmap_a, &full[stage], kb * kKPerStage, m0);
+          {
+            const int ka = kb * kKPerStage;  // A is a 3-D map (W, M, K / W): one chunk holds whole stage boxes
+            const int ja = ka / p.a_chunk;
+            tma_load_3d(sa_ptr, &tmap_a, &full[stage], ka - ja * p.a_chunk, m0, ja);
+          }
           tma_load_2d(sa_ptr + Cfg::kABytes, &tmap_b, &full[stage], kb * kKPerStage, n0);
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -417,8 +435,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
           } else if (row_ok) {
-            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n, t, n,
-                             p.N);
+            store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
           }
         }
         if (HAS_LR) {
@@ -441,8 +458,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            store_bf16_chunk(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo + n0 + c,
-                             t, n0 + c, p.N);
+            store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
           }
         }
       } else if (EPI == EPI_RAW_I32) {

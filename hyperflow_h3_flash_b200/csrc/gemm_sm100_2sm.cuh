@@ -394,6 +394,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     uint8_t* my_boxes = store_stage + (warp - 2) * 2 * Cfg::kStoreBoxBytes;
     int box_sel = 0;
     auto stage_and_store = [&](const float (&t)[32], int m_box, int n_col) {
+      // A box wholly right of N has nothing to store.  Skipping it is also what keeps every store's x coordinate
+      // 16-byte aligned: with one chunk of width N (plain layout, any N), n_col >= N would map to chunk 1 at
+      // x = n_col - N, which is 16-byte aligned only when N is a multiple of 8.  (n_col is warp-uniform.)
+      if (n_col >= p.N) return;
       uint8_t* box = my_boxes + box_sel * Cfg::kStoreBoxBytes;
       if (lane == 0) bulk_wait_group_read<1>();  // the store that used this box two chunks ago has read it
       __syncwarp();
@@ -412,7 +416,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_2d(&tmap_y, box, n_col, m_box);
+        const int jy = n_col / p.out_chunk;  // output map is 3-D (W, M, N / W); a 32-column box sits in one chunk
+        tma_store_3d(&tmap_y, box, n_col - jy * p.out_chunk, m_box, jy);
         bulk_commit_group();
       }
       box_sel ^= 1;

@@ -27,9 +27,14 @@
 
 namespace convrot {
 
+// x is read as "chunked rows": element (m, k) at x + (k / x_chunk) * x_chunk_stride + m * ldx + k % x_chunk.
+// Plain row-major input is x_chunk = K; the Ulysses receive buffer [P, M, K / P] is x_chunk = K / P, ldx = K / P,
+// x_chunk_stride = M * K / P.
 struct RotQuantParams {
   const __nv_bfloat16* x;
   int64_t ldx;
+  int x_chunk;
+  int64_t x_chunk_stride;
   int M, K;
   int8_t* q;
   int64_t ldq;
@@ -127,12 +132,19 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     fence_mbarrier_init();
   }
   __syncthreads();
+  // One bulk copy per chunk of the row (one for plain rows) into the stage's linear row buffer.
+  auto issue_row_v1 = [&](int stage, int m) {
+    mbar_arrive_expect_tx(&bars[stage], row_bytes);
+    const __nv_bfloat16* rowp = p.x + static_cast<int64_t>(m) * p.ldx;
+    for (int j = 0; j * p.x_chunk < K; ++j)
+      bulk_load(rows + static_cast<size_t>(stage) * K + j * p.x_chunk, rowp + j * p.x_chunk_stride,
+                static_cast<uint32_t>(p.x_chunk) * 2, &bars[stage]);
+  };
   if (tid == 0) {
     for (int st = 0; st < stages; ++st) {
       const int m = blockIdx.x + st * gridDim.x;
       if (m >= p.M) break;
-      mbar_arrive_expect_tx(&bars[st], row_bytes);
-      bulk_load(rows + static_cast<size_t>(st) * K, p.x + static_cast<int64_t>(m) * p.ldx, row_bytes, &bars[st]);
+      issue_row_v1(st, m);
     }
   }
 
@@ -278,11 +290,7 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     __syncthreads();  // the row buffer and warp maxima are free again
     if (tid == 0) {
       const int m_next = m + stages * gridDim.x;
-      if (m_next < p.M) {
-        mbar_arrive_expect_tx(&bars[st], row_bytes);
-        bulk_load(rows + static_cast<size_t>(st) * K, p.x + static_cast<int64_t>(m_next) * p.ldx, row_bytes,
-                  &bars[st]);
-      }
+      if (m_next < p.M) issue_row_v1(st, m_next);
     }
   }
   if (aborted && tid == 0) {
@@ -309,13 +317,23 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
 constexpr int kSlotBytes = 544;
 constexpr int kTrRow = 16 + kRQPadDoubles;  // doubles per transpose row
 
-__host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages) {
+struct RQ256Piece {
+  int64_t src0, src1;       // element offsets from the row start of the group's first and second piece
+  uint32_t bytes0, bytes1;  // bytes1 == 0: the group lies in one chunk
+};
+
+__host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages, bool chunked = false) {
   const size_t slots = static_cast<size_t>(K / 256) * kSlotBytes;
   const size_t tr = static_cast<size_t>(threads / 8) * 8 * kTrRow * 8;  // per team: 8 rows of the half transpose
-  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + 64;
+  const size_t table = chunked ? static_cast<size_t>(K / 256) * sizeof(RQ256Piece) : 0;
+  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + table + 64;
 }
 
-template <int SLOTS, int ROUNDING>
+// CHUNKED selects the chunked-row input (the Ulysses receive layout): each row's copies come from a table of
+// (source offset, bytes) pairs built once per CTA, so the per-row issue costs what the plain walk costs.  Plain rows
+// (x_chunk == K) use the instantiation without it, which compiles to 86 registers: at K = 5120 (160 threads) four
+// CTAs fit an SM, which is what the launch assumes (at most 96).
+template <int SLOTS, int ROUNDING, bool CHUNKED>
 __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantParams p) {
   extern __shared__ __align__(1024) uint8_t rq2_smem_raw[];
   const int K = p.K;
@@ -327,6 +345,8 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
   double* tr = reinterpret_cast<double*>(rq2_smem_raw + stages * stage_bytes);
   float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr / 8) * 8 * kTrRow);
   uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 32);
+  // CHUNKED: per group, the source offsets (elements from the row start) and byte counts of its one or two pieces
+  RQ256Piece* pieces = reinterpret_cast<RQ256Piece*>(bars + kRQMaxStages);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -339,16 +359,41 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
   constexpr float kScale = 1.0f / 16.0f;  // 2^-L, L = 4
 
   auto issue_row = [&](int stage, int m) {
-    // one bulk copy per group into its padded slot; all complete on the stage's barrier
+    // one bulk copy per group into its padded slot (two when the group straddles a chunk of the input layout);
+    // all complete on the stage's barrier
     mbar_arrive_expect_tx(&bars[stage], row_bytes);
     const __nv_bfloat16* src = p.x + static_cast<int64_t>(m) * p.ldx;
     uint8_t* dst = rows + stage * stage_bytes;
-    for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlotBytes, src + g * 256, 512, &bars[stage]);
+    if constexpr (!CHUNKED) {
+      for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlotBytes, src + g * 256, 512, &bars[stage]);
+    } else {
+#pragma unroll 1
+      for (int g = 0; g < ngroups; ++g) {
+        const RQ256Piece pc = pieces[g];
+        bulk_load(dst + g * kSlotBytes, src + pc.src0, pc.bytes0, &bars[stage]);
+        if (pc.bytes1) bulk_load(dst + g * kSlotBytes + pc.bytes0, src + pc.src1, pc.bytes1, &bars[stage]);
+      }
+    }
   };
 
   if (tid == 0) {
     for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
     fence_mbarrier_init();
+    if constexpr (CHUNKED) {
+      // x_chunk is a multiple of 128, so a group of 256 spans at most two chunks
+      for (int g = 0; g < ngroups; ++g) {
+        const int c0 = g * 256;
+        const int j = c0 / p.x_chunk;
+        const int c = c0 - j * p.x_chunk;
+        const int first = p.x_chunk - c < 256 ? p.x_chunk - c : 256;
+        RQ256Piece pc;
+        pc.src0 = j * p.x_chunk_stride + c;
+        pc.src1 = (j + 1) * p.x_chunk_stride;
+        pc.bytes0 = static_cast<uint32_t>(first) * 2;
+        pc.bytes1 = static_cast<uint32_t>(256 - first) * 2;
+        pieces[g] = pc;
+      }
+    }
   }
   __syncthreads();
   if (tid == 0)

@@ -162,7 +162,9 @@ class Int8RotLinear(nn.Module):
             start += layer.rank
         return fused[:, start:start + self.rank]
 
-    def forward(self, x: Tensor) -> Tensor:
+    def forward(self, x: Tensor, *, out_chunks: int | None = None) -> Tensor:
+        """``out_chunks = P`` (CUDA only) returns the output packed for the Ulysses all-to-all: ``[P, M, N / P]``,
+        column block j of every row in ``[j]`` (see ``forward_packed`` for the matching input)."""
         shape = x.shape
         x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
         if x2.is_cuda:
@@ -175,8 +177,12 @@ class Int8RotLinear(nn.Module):
                 xq, sx = kernels.rotate_quant_torch_rounding(x2, self.group)
             xa = self._lowrank_input(x2, kernels) if self.rank else None
             y = kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
-                                       up=self.up.weight if self.rank else None)
+                                       up=self.up.weight if self.rank else None, out_chunks=out_chunks)
+            if out_chunks:
+                return y
         else:
+            if out_chunks:
+                raise ValueError("packed outputs are produced on CUDA tensors only")
             Int8RotLinear._last_input.clear()
             y = self._forward_torch(x2, _rotation(self.group, x2.device))
             if self.bias is not None:
@@ -184,6 +190,22 @@ class Int8RotLinear(nn.Module):
             if self.rank:
                 y = y + self.up(self.down(x2))
         return y.reshape(*shape[:-1], self.out_features).to(x.dtype)
+
+    def forward_packed(self, xp: Tensor, *, out_chunks: int | None = None) -> Tensor:
+        """The layer on an input packed as ``[P, M, K / P]`` -- row m is ``cat(xp[0, m], ..., xp[P-1, m])``, the
+        receive buffer of the Ulysses head -> seq all-to-all -- without unpacking it (CUDA only)."""
+        if not xp.is_cuda or xp.dim() != 3 or xp.shape[0] * xp.shape[2] != self.in_features:
+            raise ValueError(f"expected a CUDA tensor [P, M, {self.in_features} / P], got {tuple(xp.shape)}")
+        xp = xp.to(torch.bfloat16).contiguous()
+        kernels = _kernels()
+        Int8RotLinear._last_input.clear()
+        self._lowrank_hit = None
+        rows = xp.shape[1]
+        rounding = _lib.ROUND_KERNEL if rows >= _MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+        xq, sx = kernels.rotate_quant_packed(xp, self.group, rounding)
+        xa = kernels.lowrank_down_packed(xp, self.down.weight) if self.rank else None
+        return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
+                                      up=self.up.weight if self.rank else None, out_chunks=out_chunks)
 
     def _forward_torch(self, x2: Tensor, rot: Tensor) -> Tensor:
         """The reference's torch path (int8.py:173-179): the rotation is rounded to bf16 and the codes divide by
@@ -259,6 +281,37 @@ def rotate_quant(x: Tensor, group: int, rounding: int = _lib.ROUND_KERNEL) -> tu
     return (q if Kp == K else q[:, :K]), s
 
 
+def rotate_quant_packed(xp: Tensor, group: int, rounding: int = _lib.ROUND_KERNEL) -> tuple[Tensor, Tensor]:
+    """``rotate_quant`` of the rows of a packed ``[P, M, K / P]`` input (the Ulysses receive layout)."""
+    _require(xp, "xp", torch.bfloat16, 3)
+    P, M, W = xp.shape
+    K = P * W
+    xp = xp.contiguous()
+    q = torch.empty(M, K, dtype=torch.int8, device=xp.device)
+    s = torch.empty(M, dtype=torch.float32, device=xp.device)
+    rc = _lib.lib().convrot_rotate_quant_packed(_ptr(xp), W, M, K, group, rounding, _ptr(q), K, _ptr(s),
+                                                _stream(xp))
+    _lib.check(rc, "convrot_rotate_quant_packed")
+    return q, s
+
+
+def lowrank_down_packed(xp: Tensor, down: Tensor) -> Tensor:
+    """``bf16(x . down^T)`` for a packed ``[P, M, K / P]`` input."""
+    _require(xp, "xp", torch.bfloat16, 3)
+    _require(down, "down", torch.bfloat16, 2)
+    P, M, W = xp.shape
+    K = P * W
+    r = down.shape[0]
+    xp = xp.contiguous()
+    down = down.contiguous()
+    ld = -(-r // 8) * 8
+    xa = torch.empty(M, ld, dtype=torch.bfloat16, device=xp.device)
+    rc = _lib.lib().convrot_lowrank_down_packed(_ptr(xp), W, _ptr(down), down.stride(0), M, K, r, _ptr(xa), ld,
+                                                _stream(xp))
+    _lib.check(rc, "convrot_lowrank_down_packed")
+    return xa if ld == r else xa[:, :r]
+
+
 def rotate_quant_torch_rounding(x: Tensor, group: int) -> tuple[Tensor, Tensor]:
     """``rotate_quant`` with the reference torch path's rounding (bf16 rotation, division): int8.py:175-178."""
     return rotate_quant(x, group, _lib.ROUND_TORCH)
@@ -284,8 +337,10 @@ def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
 
 
 def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor | None = None,
-                   xa: Tensor | None = None, up: Tensor | None = None) -> Tensor:
-    """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions)."""
+                   xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None) -> Tensor:
+    """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
+
+    ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout)."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -315,6 +370,17 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         lr = -(-r // 8) * 8
         xa = _pad_cols(xa.to(torch.bfloat16), lr)
         up = _pad_cols(up.to(torch.bfloat16).contiguous(), lr)
+    if out_chunks:
+        if N % out_chunks:
+            raise ValueError(f"N = {N} does not split into {out_chunks} chunks")
+        W = N // out_chunks
+        y = torch.empty(out_chunks, M, W, dtype=torch.bfloat16, device=a.device)
+        rc = _lib.lib().convrot_gemm_packed(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                            _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                            up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(y), W,
+                                            _stream(a))
+        _lib.check(rc, "convrot_gemm_packed")
+        return y
     ldy = -(-N // 8) * 8
     y = torch.empty(M, ldy, dtype=torch.bfloat16, device=a.device)
     rc = _lib.lib().convrot_gemm(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
@@ -357,6 +423,8 @@ def _kernels() -> SimpleNamespace:
         convrot_matmul=convrot_matmul,
         lowrank_down=lowrank_down,
         int8_mm_acc=int8_mm_acc,
+        rotate_quant_packed=rotate_quant_packed,
+        lowrank_down_packed=lowrank_down_packed,
     )
 
 

@@ -98,6 +98,25 @@ int convrot_gemm_acc(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
                      int64_t K, int32_t* acc, int64_t ldc, void* stream);
 
 /*
+ * Packed layouts of the Ulysses all-to-all (no counterpart in the reference, whose all-to-all lives in diffusers;
+ * call site distributed.py:88-96).  A packed bf16 matrix [M, C] with chunk_cols = W is stored as [C / W, M, W]:
+ * element (m, c) at base[(c / W) * M * W + m * W + c % W] -- all M rows of column block 0, then block 1, ...
+ * This is exactly the send buffer of all_to_all_single for seq -> head (block j goes to rank j) and the receive
+ * buffer of head -> seq (block j came from rank j), so no pack or unpack copy is needed around the collective.
+ *
+ * convrot_gemm_packed         as convrot_gemm, writing y packed (N % chunk_cols == 0, chunk_cols % 32 == 0)
+ * convrot_rotate_quant_packed as convrot_rotate_quant, reading x packed (K % chunk_cols == 0, chunk_cols % 128 == 0)
+ * convrot_lowrank_down_packed as convrot_lowrank_down, reading x packed (chunk_cols % 64 == 0)
+ */
+int convrot_gemm_packed(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                        const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                        int64_t M, int64_t N, int64_t K, void* y, int64_t chunk_cols, void* stream);
+int convrot_rotate_quant_packed(const void* x, int64_t chunk_cols, int64_t M, int64_t K, int group, int rounding,
+                                int8_t* q_out, int64_t ldq, float* s_out, void* stream);
+int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* lr_down, int64_t ld_down, int64_t M,
+                                int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
+
+/*
  * Workspace for convrot_linear: q (int8 [M, K]), s (fp32 [M]) and xa (bf16 [M, r]), each 256-byte aligned.
  */
 size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r);

@@ -358,3 +358,57 @@ def test_convrot_linear_with_a_workspace_matches_the_module(M, K, N, r):
         assert torch.equal(y, ref)
     else:  # the module reproduces the reference's torch-path rounding below 17 rows; the C entry does not
         assert close(y.float().cpu().numpy(), ref.float().cpu().numpy())[1] >= 0.9999
+
+
+def pack(x: torch.Tensor, P: int) -> torch.Tensor:
+    """[M, K] -> [P, M, K / P]: column block j of every row in [j] (the Ulysses all-to-all layout)."""
+    M, K = x.shape
+    return x.reshape(M, P, K // P).transpose(0, 1).contiguous()
+
+
+@pytest.mark.parametrize("M,N,K,r,P", [
+    (333, 5120, 5120, 32, 8), (4096, 2048, 1024, 0, 2), (1000, 1536, 512, 64, 4), (17, 640, 256, 16, 2),
+])
+def test_packed_gemm_output_is_the_plain_output_in_blocks(M, N, K, r, P, gemm_mode):
+    """convrot_gemm_packed writes the same bits as convrot_gemm, column block j of each row to [j]."""
+    x = synthetic.activations(M, K, seed=51).to(DEV)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256).to(DEV)
+    q, s = I.rotate_quant(x, 256)
+    xa = I.lowrank_down(x, w.down) if r else None
+    up = w.up if r else None
+    plain = I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=up)
+    packed = I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=up, out_chunks=P)
+    assert packed.shape == (P, M, N // P)
+    assert torch.equal(packed, pack(plain, P))
+
+
+@pytest.mark.parametrize("M,K,P,group", [(333, 5120, 8, 256), (1000, 4096, 2, 256), (64, 1024, 4, 64),
+                                         (8, 5120, 8, 256), (16, 2048, 2, 16)])
+def test_packed_rotate_and_down_projection_equal_the_plain_ones(M, K, P, group, rotate_variant):
+    """The kernels reading the packed [P, M, K/P] receive layout give the plain layout's codes, scales and x.A."""
+    x = synthetic.activations(M, K, seed=52).to(DEV)
+    xp = pack(x, P)
+    rounding = _lib.ROUND_KERNEL if M >= I._MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+    if rounding == _lib.ROUND_KERNEL:
+        q, s = I.rotate_quant(x, group)
+    else:
+        q, s = I.rotate_quant_torch_rounding(x, group)
+    qp, sp = I.rotate_quant_packed(xp, group, rounding)
+    assert torch.equal(q, qp) and torch.equal(s, sp)
+    down = synthetic.linear_weights(K, 64, rank=48, bias=False, group=256).down.to(DEV)
+    assert torch.equal(I.lowrank_down(x, down), I.lowrank_down_packed(xp, down))
+
+
+@pytest.mark.parametrize("M,K,N,r,P", [(333, 5120, 5120, 32, 8), (40, 1024, 2048, 0, 2), (9, 2048, 512, 16, 4)])
+def test_layer_packed_forms_equal_the_plain_forward(M, K, N, r, P):
+    """Int8RotLinear: forward(x, out_chunks=P) is forward(x) packed; forward_packed(pack(x)) is forward(x)."""
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256)
+    layer = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+    synthetic.load_into(layer, w)
+    layer = layer.to(DEV)
+    x = synthetic.activations(M, K, seed=53).to(DEV)
+    ref = layer(x)
+    assert torch.equal(layer(x, out_chunks=P), pack(ref, P))
+    assert torch.equal(layer.forward_packed(pack(x, P)), ref)
+    with pytest.raises(ValueError):
+        layer.forward_packed(x)
