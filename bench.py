@@ -48,6 +48,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--rows", type=int, default=32768, help="token rows per rank")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                    help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--case", choices=["gemm", "gemm_plain", "rotate", "down"], default=None,
                     help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
     return ap.parse_args()
@@ -234,7 +236,7 @@ class KernelTimer:
                 self.gemm_shapes.append((a[0].shape[0], a[1].shape[0], a[0].shape[1]))
             elif kind == "rq":
                 self.rq_events.append((s, e))
-                self.rq_shapes.append(tuple(a[0].shape))
+                self.rq_shapes.append(tuple(getattr(a[0], "shape", ())))
             return out
 
         setattr(self.kernels, name, wrapped)
@@ -246,6 +248,7 @@ class KernelTimer:
         self._wrap("lowrank_down", "down", 1)
         self._wrap("rotate_quant_packed", "rq", 1)
         self._wrap("lowrank_down_packed", "down", 1)
+        self._wrap("rotate_quant_gather", "rq", 1)
         return self
 
     def __exit__(self, *exc):
@@ -294,8 +297,12 @@ def run_ours(args) -> None:
     x = x_host.to(dev)
     y_host = torch.empty(M, N_DIM, dtype=torch.bfloat16).pin_memory()
 
+    exchange = None
+    if world > 1 and args.transport == "peer":
+        exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev)
+
     def step(inp):
-        return ulysses.attention_block_linears(inp, to_q, to_k, to_v, to_out, HEADS)
+        return ulysses.attention_block_linears(inp, to_q, to_k, to_v, to_out, HEADS, exchange=exchange)
 
     kernels = I._kernels()
     timer = KernelTimer(torch, kernels)
@@ -307,6 +314,7 @@ def run_ours(args) -> None:
         barrier()
         timer.active = True
         timer.reset()
+        exchange_launches = exchange.kernel_launches if exchange else 0
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local) as clocks:
             torch.cuda.synchronize()
@@ -321,7 +329,7 @@ def run_ours(args) -> None:
         ms = start.elapsed_time(end)
         gemm_ms = [s.elapsed_time(e) for s, e in timer.gemm_events]
         rq_ms = [s.elapsed_time(e) for s, e in timer.rq_events]
-        launches = timer.launches
+        launches = timer.launches + (exchange.kernel_launches - exchange_launches if exchange else 0)
         t = torch.tensor([ms], device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -377,9 +385,11 @@ def run_ours(args) -> None:
             "config": {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
                                    f"M={M} rows/rank, K=N={K_DIM}, r={RANK}, bias, group {GROUP}"
                                    + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity "
-                                      "attention" if world > 1 else ""),
+                                      "attention" + (" (fused into the kernels over peer memory)"
+                                                     if exchange else " (NCCL)") if world > 1 else ""),
                        "rows_per_rank": M, "total_rows": M * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
                        "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
+                       "transport": (args.transport if world > 1 else None),
                        "l2": "inputs larger than L2 (x is 335 MB per step), no flush"},
             "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2,
@@ -397,6 +407,8 @@ def run_ours(args) -> None:
             line["rotate_quant"]["frac"] = line["rotate_quant"]["achieved_gbs"] / line["rotate_quant"]["peak_gbs"]
         line.update(extras)
         print(json.dumps(line), flush=True)
+    if exchange is not None:
+        exchange.close()
     if world > 1:
         dist.destroy_process_group()
 

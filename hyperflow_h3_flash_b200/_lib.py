@@ -18,6 +18,8 @@ NOALLOC_SCRATCH_BYTES = 16 << 20
 ROUND_KERNEL, ROUND_TORCH = 0, 1
 
 _P, _I, _L, _S, _U64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
+_U32 = ctypes.c_uint32
+IPC_HANDLE_BYTES = 64
 
 #: Every exported function with its argument types, in header order.
 SIGNATURES: dict[str, tuple[list, object]] = {
@@ -28,6 +30,13 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_gemm_packed": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_rotate_quant_packed": ([_P, _L, _L, _L, _I, _I, _P, _L, _P, _P], _I),
     "convrot_lowrank_down_packed": ([_P, _L, _P, _L, _L, _L, _L, _P, _L, _P], _I),
+    "convrot_gemm_scatter": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _I, _L, _P], _I),
+    "convrot_rotate_quant_gather": ([_P, _I, _L, _L, _L, _I, _I, _P, _L, _P, _P, _L, _P], _I),
+    "convrot_ipc_handle": ([_P, _P, _P], _I),
+    "convrot_ipc_open": ([_P, _P], _I),
+    "convrot_ipc_close": ([_P], _I),
+    "convrot_peer_signal": ([_P, _I, _U32, _P], _I),
+    "convrot_peer_wait": ([_P, _I, _U32, _P], _I),
     "convrot_workspace_size": ([_L, _L, _L], _S),
     "convrot_linear": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _S, _P, _L, _P], _I),
     "convrot_linear_noalloc": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _L, _P], _I),

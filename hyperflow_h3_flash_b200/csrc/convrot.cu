@@ -15,6 +15,7 @@
 #include "../../include/convrot.h"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_2sm.cuh"
+#include "peer.cuh"
 #include "rotate_quant.cuh"
 
 namespace convrot {
@@ -51,6 +52,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddressRangeFn g_address_range = nullptr;
 
 int cuda_fail(cudaError_t e) {
   t_last_cuda_error = static_cast<int>(e);
@@ -81,6 +84,14 @@ int device_state(DeviceState** out) {
           return cuda_fail(e);
         if (q != cudaDriverEntryPointSuccess || !fn) return CONVROT_ERR_CUDA;
         g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+      }
+      if (!g_address_range) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if ((e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q)) != cudaSuccess)
+          return cuda_fail(e);
+        if (q != cudaDriverEntryPointSuccess || !fn) return CONVROT_ERR_CUDA;
+        g_address_range = reinterpret_cast<AddressRangeFn>(fn);
       }
     }
     st.ready = true;
@@ -194,7 +205,7 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
 
 template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
 int launch_gemm2(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& txa,
-                 const CUtensorMap& tup, const CUtensorMap& ty, const GemmParams& p, cudaStream_t stream) {
+                 const CUtensorMap& tup, const OutMaps& ty, const GemmParams& p, cudaStream_t stream) {
   auto kernel = convrot_gemm2sm_kernel<Cfg, EPI, LR_ATOM, LR_ATOMS>;
   const int pair_tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
   int clusters = -1;
@@ -230,13 +241,22 @@ using Cfg2 = Gemm2Cfg<5, 0, 0>;
 using Cfg2LR32 = Gemm2Cfg<5, 64, 1>;
 using Cfg2LR64 = Gemm2Cfg<5, 128, 1>;
 
-// out_chunk > 0 writes the bf16 output as [N / out_chunk, M, out_chunk] (the Ulysses send layout) and ignores ldo.
+// n_chunks > 1 writes the bf16 output in column chunks of N / n_chunks: chunk j as [M, ldo] rows at chunks[j] (the
+// Ulysses send layout, or the receive buffers of the other GPUs); `out` is then ignored.
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
-            int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream, int64_t out_chunk = 0) {
-  if (out_chunk > 0) {
-    if (raw || out_chunk % 32 || N % out_chunk) return CONVROT_ERR_SHAPE;
-    ldo = out_chunk;
+            int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream,
+            void* const* chunks = nullptr, int n_chunks = 1) {
+  if (n_chunks < 1 || n_chunks > kMaxChunks || (n_chunks > 1 && !chunks)) return CONVROT_ERR_ARG;
+  int64_t out_chunk = N;
+  if (n_chunks > 1) {
+    if (raw || N % n_chunks || (N / n_chunks) % 32) return CONVROT_ERR_SHAPE;
+    out_chunk = N / n_chunks;
+    for (int j = 0; j < n_chunks; ++j) {
+      if (!chunks[j]) return CONVROT_ERR_ARG;
+      if (!aligned16(chunks[j])) return CONVROT_ERR_ALIGN;
+    }
+    out = chunks[0];
   }
   if (M < 0 || N <= 0 || K <= 0) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
@@ -246,7 +266,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   const bool has_lr = !raw && xa && up && r > 0;
   if (!raw && (xa || up) && !has_lr) return CONVROT_ERR_ARG;
   if (has_lr && r > 64) return CONVROT_ERR_SHAPE;
-  if (K % 16 || ldq < K || ldw < K || ldo < (out_chunk > 0 ? out_chunk : N)) return CONVROT_ERR_SHAPE;
+  if (K % 16 || ldq < K || ldw < K || ldo < out_chunk) return CONVROT_ERR_SHAPE;
   if (ldq % 16 || ldw % 16 || !aligned16(q) || !aligned16(w)) return CONVROT_ERR_ALIGN;
   if (raw ? (ldo % 4 || !aligned16(out)) : (ldo % 8 || !aligned16(out))) return CONVROT_ERR_ALIGN;
   if (!raw && (!aligned16(ws) || (bias && !aligned16(bias)))) return CONVROT_ERR_ALIGN;
@@ -282,19 +302,19 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.sb = ws;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.out = out;
+  for (int j = 0; j < kMaxChunks; ++j) p.out_chunks[j] = j < n_chunks ? (n_chunks > 1 ? chunks[j] : out) : nullptr;
   p.ldo = ldo;
-  p.out_chunk = out_chunk > 0 ? static_cast<int>(out_chunk) : static_cast<int>(N);
-  p.out_chunk_stride = out_chunk > 0 ? M * out_chunk : 0;
+  p.out_chunk = static_cast<int>(out_chunk);
   p.a_chunk = static_cast<int>(K);
   p.r = has_lr ? static_cast<int>(r) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   if (two_sm) {
-    CUtensorMap ty;  // bf16 output, 32 x 32 boxes for the epilogue's TMA stores
+    OutMaps ty;  // bf16 output, one map per chunk, 32 x 32 boxes for the epilogue's TMA stores
     memset(&ty, 0, sizeof(ty));
-    if (!raw && (rc = make_map3(&ty, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, p.out_chunk, N / p.out_chunk,
-                                ldo, p.out_chunk_stride, 32, 32)))
-      return rc;
+    for (int j = 0; j < n_chunks && !raw; ++j)
+      if ((rc = make_map(&ty.m[j], p.out_chunks[j], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, out_chunk, ldo, 32, 32)))
+        return rc;
     if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
     if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
     if (lr_atom == 64) return launch_gemm2<Cfg2LR32, EPI_DEQUANT, 64, 1>(*st, ta, tb, txa, tup, ty, p, stream);
@@ -338,9 +358,9 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
   p.N = static_cast<int>(r);
   p.K = static_cast<int>(K);
   p.out = xa;
+  p.out_chunks[0] = xa;
   p.ldo = ldxa;
   p.out_chunk = static_cast<int>(r);
-  p.out_chunk_stride = 0;
   p.a_chunk = static_cast<int>(x_chunk);
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
@@ -415,6 +435,7 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
   const bool chunked = p.x_chunk != p.K;
+  if (chunked && slots == 1 && threads > kRQ256ChunkedThreads) return launch_rq<256>(st, p, stream);
   const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
   void (*kernel)(const RotQuantParams) = nullptr;
   if (slots == 1 && !chunked)
@@ -464,26 +485,44 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
 
+// Row m of x is the concatenation of chunk j's row m over j (n_chunks chunks of K / n_chunks columns, rows ldx
+// apart); one chunk is plain row-major x.  x_out (optional, chunked input only) receives each gathered row.
 int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding, int8_t* q, int64_t ldq,
-                 float* s, cudaStream_t stream, int64_t x_chunk = 0, int64_t x_chunk_stride = 0) {
-  if (x_chunk <= 0) x_chunk = K;
-  if (x_chunk != K && (K % x_chunk || x_chunk % 128 || x_chunk_stride % 8 || x_chunk > INT32_MAX))
-    return CONVROT_ERR_SHAPE;
+                 float* s, cudaStream_t stream, const void* const* chunks = nullptr, int n_chunks = 1,
+                 void* x_out = nullptr, int64_t ld_out = 0) {
+  if (n_chunks < 1 || n_chunks > kMaxChunks || (n_chunks > 1 && !chunks)) return CONVROT_ERR_ARG;
   if (M < 0 || K <= 0) return CONVROT_ERR_SHAPE;
+  const int64_t x_chunk = K / n_chunks;
+  if (n_chunks > 1) {
+    if (K % n_chunks || x_chunk % 128) return CONVROT_ERR_SHAPE;
+    for (int j = 0; j < n_chunks; ++j) {
+      if (!chunks[j]) return CONVROT_ERR_ARG;
+      if (!aligned16(chunks[j])) return CONVROT_ERR_ALIGN;
+    }
+    x = chunks[0];
+  } else if (x_out) {
+    return CONVROT_ERR_ARG;  // a plain row-major x is already what x_out would hold
+  }
   if (group != 4 && group != 16 && group != 64 && group != 256) return CONVROT_ERR_GROUP;
   if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
   if (K % group || K % 16 || K > 32768 || ldx < x_chunk || ldq < K || M > INT32_MAX) return CONVROT_ERR_SHAPE;
+  if (x_out && ld_out < K) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
   if (!x || !q || !s) return CONVROT_ERR_ARG;
   if (ldx % 8 || ldq % 16 || !aligned16(x) || !aligned16(q)) return CONVROT_ERR_ALIGN;
+  if (x_out && (ld_out % 8 || !aligned16(x_out))) return CONVROT_ERR_ALIGN;
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
   RotQuantParams p;
+  memset(&p, 0, sizeof(p));
   p.x = static_cast<const __nv_bfloat16*>(x);
+  for (int j = 0; j < n_chunks; ++j)
+    p.xs[j] = static_cast<const __nv_bfloat16*>(n_chunks > 1 ? chunks[j] : x);
   p.ldx = ldx;
   p.x_chunk = static_cast<int>(x_chunk);
-  p.x_chunk_stride = x_chunk_stride;
+  p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  p.ld_out = ld_out;
   p.M = static_cast<int>(M);
   p.K = static_cast<int>(K);
   p.q = q;
@@ -553,9 +592,21 @@ int convrot_rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int g
 
 int convrot_rotate_quant_packed(const void* x, int64_t chunk_cols, int64_t M, int64_t K, int group, int rounding,
                                 int8_t* q_out, int64_t ldq, float* s_out, void* stream) {
-  if (chunk_cols <= 0 || M < 0) return CONVROT_ERR_SHAPE;
+  if (chunk_cols <= 0 || M < 0 || K % chunk_cols || K / chunk_cols > kMaxChunks) return CONVROT_ERR_SHAPE;
+  if (!x) return CONVROT_ERR_ARG;
+  const void* chunks[kMaxChunks];
+  const int n = static_cast<int>(K / chunk_cols);
+  for (int j = 0; j < n; ++j) chunks[j] = static_cast<const uint8_t*>(x) + j * M * chunk_cols * 2;
   return rotate_quant(x, chunk_cols, M, K, group, rounding, q_out, ldq, s_out, static_cast<cudaStream_t>(stream),
-                      chunk_cols, M * chunk_cols);
+                      chunks, n);
+}
+
+int convrot_rotate_quant_gather(const void* const* x_chunks, int n_chunks, int64_t ldx, int64_t M, int64_t K,
+                                int group, int rounding, int8_t* q_out, int64_t ldq, float* s_out, void* x_out,
+                                int64_t ld_out, void* stream) {
+  if (n_chunks < 2) return CONVROT_ERR_ARG;
+  return rotate_quant(nullptr, ldx, M, K, group, rounding, q_out, ldq, s_out, static_cast<cudaStream_t>(stream),
+                      x_chunks, n_chunks, x_out, ld_out);
 }
 
 int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* lr_down, int64_t ld_down, int64_t M,
@@ -568,9 +619,86 @@ int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* l
 int convrot_gemm_packed(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
                         const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
                         int64_t M, int64_t N, int64_t K, void* y, int64_t chunk_cols, void* stream) {
-  if (chunk_cols <= 0) return CONVROT_ERR_SHAPE;
+  if (chunk_cols <= 0 || M < 0 || N % chunk_cols || N / chunk_cols > kMaxChunks) return CONVROT_ERR_SHAPE;
+  if (!y) return CONVROT_ERR_ARG;
+  void* chunks[kMaxChunks];
+  const int n = static_cast<int>(N / chunk_cols);
+  for (int j = 0; j < n; ++j) chunks[j] = static_cast<uint8_t*>(y) + j * M * chunk_cols * 2;
   return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, chunk_cols, false,
-                 static_cast<cudaStream_t>(stream), chunk_cols);
+                 static_cast<cudaStream_t>(stream), chunks, n);
+}
+
+int convrot_gemm_scatter(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                         const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                         int64_t M, int64_t N, int64_t K, void* const* y_chunks, int n_chunks, int64_t ldy,
+                         void* stream) {
+  if (n_chunks < 2) return CONVROT_ERR_ARG;
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, nullptr, ldy, false,
+                 static_cast<cudaStream_t>(stream), y_chunks, n_chunks);
+}
+
+int convrot_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return CONVROT_ERR_ARG;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = g_address_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) {
+    t_last_cuda_error = static_cast<int>(r);
+    return CONVROT_ERR_CUDA;
+  }
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e);
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return CONVROT_OK;
+}
+
+int convrot_ipc_open(const void* handle, void** base_out) {
+  if (!handle || !base_out) return CONVROT_ERR_ARG;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+int convrot_ipc_close(void* base) {
+  if (!base) return CONVROT_ERR_ARG;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+int convrot_peer_signal(uint32_t* const* slots, int n, uint32_t epoch, void* stream) {
+  if (n < 1 || n > kMaxChunks || !slots) return CONVROT_ERR_ARG;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  PeerSlots ps;
+  memset(&ps, 0, sizeof(ps));
+  for (int j = 0; j < n; ++j) {
+    if (!slots[j] || (reinterpret_cast<uintptr_t>(slots[j]) & 3u)) return CONVROT_ERR_ARG;
+    ps.slot[j] = slots[j];
+  }
+  peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ps, n, epoch);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
+int convrot_peer_wait(const uint32_t* flags, int n, uint32_t epoch, void* stream) {
+  if (n < 1 || n > kMaxChunks || !flags || (reinterpret_cast<uintptr_t>(flags) & 3u)) return CONVROT_ERR_ARG;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  peer_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(flags, n, epoch, g_wait_limit_ns,
+                                                                   st->error_word);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
 
 int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down, int64_t M, int64_t K,

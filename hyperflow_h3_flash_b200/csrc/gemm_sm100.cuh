@@ -41,10 +41,10 @@ struct GemmParams {
   const float* sa;      // [M]   (EPI_DEQUANT)
   const float* sb;      // [N]   (EPI_DEQUANT)
   const __nv_bfloat16* bias;  // [N] or null
-  void* out;            // bf16 [M, N] or int32 [M, N]
-  int64_t ldo;          // elements (row pitch L of the output)
-  int out_chunk;        // W of the output (N for plain rows)
-  int64_t out_chunk_stride;  // S of the output (elements)
+  void* out;            // bf16 [M, N] or int32 [M, N] (plain rows)
+  void* out_chunks[kMaxChunks];  // bf16 output in column chunks of out_chunk: chunk j is [M, ldo] rows at [j]
+  int64_t ldo;          // elements (row pitch of the output, or of each chunk)
+  int out_chunk;        // columns per chunk (N for plain rows, out_chunks[0] == out)
   int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
   uint64_t wait_limit_ns;
@@ -55,7 +55,7 @@ struct GemmParams {
 template <class T>
 __device__ __forceinline__ T* out_ptr(const GemmParams& p, int row, int n) {
   const int j = n / p.out_chunk;
-  return reinterpret_cast<T*>(p.out) + j * p.out_chunk_stride + static_cast<int64_t>(row) * p.ldo +
+  return reinterpret_cast<T*>(select_chunk(p.out_chunks, j)) + static_cast<int64_t>(row) * p.ldo +
          (n - j * p.out_chunk);
 }
 

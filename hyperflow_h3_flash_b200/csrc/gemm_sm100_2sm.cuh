@@ -146,11 +146,16 @@ struct Gemm2Cfg {
   static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 256);
 };
 
+// One bf16 output map per column chunk (box 32 x 32): chunk j covers columns [j W, (j + 1) W) of the result.
+struct OutMaps {
+  CUtensorMap m[kMaxChunks];
+};
+
 template <class Cfg, int EPI, int LR_ATOM, int LR_ATOMS>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     convrot_gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            const __grid_constant__ CUtensorMap tmap_xa, const __grid_constant__ CUtensorMap tmap_up,
-                           const __grid_constant__ CUtensorMap tmap_y, const GemmParams p) {
+                           const __grid_constant__ OutMaps tmap_y, const GemmParams p) {
   constexpr int BN = Cfg::kBN;
   constexpr int S = Cfg::kStages;
   constexpr bool HAS_LR = Cfg::kHasLR;
@@ -394,9 +399,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     uint8_t* my_boxes = store_stage + (warp - 2) * 2 * Cfg::kStoreBoxBytes;
     int box_sel = 0;
     auto stage_and_store = [&](const float (&t)[32], int m_box, int n_col) {
-      // A box wholly right of N has nothing to store.  Skipping it is also what keeps every store's x coordinate
-      // 16-byte aligned: with one chunk of width N (plain layout, any N), n_col >= N would map to chunk 1 at
-      // x = n_col - N, which is 16-byte aligned only when N is a multiple of 8.  (n_col is warp-uniform.)
+      // A box wholly right of N has nothing to store; skipping it also keeps jy inside the maps that exist (with
+      // one chunk of width N, n_col >= N would name chunk 1).  n_col is warp-uniform.
       if (n_col >= p.N) return;
       uint8_t* box = my_boxes + box_sel * Cfg::kStoreBoxBytes;
       if (lane == 0) bulk_wait_group_read<1>();  // the store that used this box two chunks ago has read it
@@ -416,8 +420,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        const int jy = n_col / p.out_chunk;  // output map is 3-D (W, M, N / W); a 32-column box sits in one chunk
-        tma_store_3d(&tmap_y, box, n_col - jy * p.out_chunk, m_box, jy);
+        const int jy = n_col / p.out_chunk;  // one 2-D map per output chunk; a 32-column box sits in one chunk
+        tma_store_2d(&tmap_y.m[jy], box, n_col - jy * p.out_chunk, m_box);
         bulk_commit_group();
       }
       box_sel ^= 1;

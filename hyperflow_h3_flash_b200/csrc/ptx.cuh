@@ -90,20 +90,19 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 3-D tiled store of one box from shared memory to global (bulk-group completion); out-of-bounds parts clipped.
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
 // 2-D tiled store of one box from shared memory to global (bulk-group completion).  Out-of-bounds parts of the box
 // are clipped by the hardware; coordinates are never negative here.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+// Untiled bulk copy shared -> global (bulk-group completion): both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(reinterpret_cast<uint64_t>(gdst)),
+               "r"(smem_u32(smem_src)), "r"(bytes)
                : "memory");
 }
 
@@ -117,6 +116,31 @@ __device__ __forceinline__ void bulk_wait_group_read() {
 
 // Wait until every bulk group of this thread has completed (its writes are done).
 __device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Flags another GPU reads or writes (the Ulysses exchange): release/acquire at system scope.
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(addr)), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(reinterpret_cast<uint64_t>(addr)) : "memory");
+  return v;
+}
+
+// Operands split into column chunks that live at independent addresses (each may be another GPU's buffer, mapped
+// into this process): at most one chunk per rank of a node.
+constexpr int kMaxChunks = 8;
+
+// tab[j] without dynamic indexing of a kernel-parameter array (which would go through local memory).
+template <class T>
+__device__ __forceinline__ T select_chunk(const T (&tab)[kMaxChunks], int j) {
+  T r = tab[0];
+#pragma unroll
+  for (int i = 1; i < kMaxChunks; ++i)
+    if (j == i) r = tab[i];
+  return r;
+}
 
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -27,14 +27,16 @@
 
 namespace convrot {
 
-// x is read as "chunked rows": element (m, k) at x + (k / x_chunk) * x_chunk_stride + m * ldx + k % x_chunk.
-// Plain row-major input is x_chunk = K; the Ulysses receive buffer [P, M, K / P] is x_chunk = K / P, ldx = K / P,
-// x_chunk_stride = M * K / P.
+// x is read as "chunked rows": element (m, k) at xs[k / x_chunk] + m * ldx + k % x_chunk.  Plain row-major input is
+// one chunk (x_chunk = K, xs[0] = x).  The Ulysses receive buffer [P, M, K / P] is P chunks of K / P columns; so is
+// the same data left in the P senders' buffers, when the kernel gathers each row straight from the other GPUs.
 struct RotQuantParams {
   const __nv_bfloat16* x;
+  const __nv_bfloat16* xs[kMaxChunks];
   int64_t ldx;
   int x_chunk;
-  int64_t x_chunk_stride;
+  __nv_bfloat16* x_out;  // optional: each gathered bf16 row is also stored to x_out + m * ld_out (null: not)
+  int64_t ld_out;
   int M, K;
   int8_t* q;
   int64_t ldq;
@@ -135,9 +137,10 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
   // One bulk copy per chunk of the row (one for plain rows) into the stage's linear row buffer.
   auto issue_row_v1 = [&](int stage, int m) {
     mbar_arrive_expect_tx(&bars[stage], row_bytes);
-    const __nv_bfloat16* rowp = p.x + static_cast<int64_t>(m) * p.ldx;
-    for (int j = 0; j * p.x_chunk < K; ++j)
-      bulk_load(rows + static_cast<size_t>(stage) * K + j * p.x_chunk, rowp + j * p.x_chunk_stride,
+    const int64_t roff = static_cast<int64_t>(m) * p.ldx;
+    int j = 0;
+    for (int k0 = 0; k0 < K; k0 += p.x_chunk, ++j)
+      bulk_load(rows + static_cast<size_t>(stage) * K + k0, select_chunk(p.xs, j) + roff,
                 static_cast<uint32_t>(p.x_chunk) * 2, &bars[stage]);
   };
   if (tid == 0) {
@@ -159,6 +162,10 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     volatile int never = 0;
     const bool arrived = mbar_wait_bounded(&bars[st], parity, p.wait_limit_ns, &never);
     const __nv_bfloat16* xr = rows + static_cast<size_t>(st) * K;
+    if (tid == 0 && p.x_out && arrived) {  // the gathered row, as it landed
+      bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out, xr, row_bytes);
+      bulk_commit_group();
+    }
 
     float y[SLOTS][16];
     float amax = 0.0f;
@@ -290,9 +297,11 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     __syncthreads();  // the row buffer and warp maxima are free again
     if (tid == 0) {
       const int m_next = m + stages * gridDim.x;
+      if (p.x_out) bulk_wait_group_read<0>();  // the row store has read this buffer
       if (m_next < p.M) issue_row_v1(st, m_next);
     }
   }
+  if (tid == 0 && p.x_out) bulk_wait_group_all();
   if (aborted && tid == 0) {
     // Let the row copies still in flight land before the CTA leaves (bounded as well).
     volatile int never = 0;
@@ -317,9 +326,14 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
 constexpr int kSlotBytes = 544;
 constexpr int kTrRow = 16 + kRQPadDoubles;  // doubles per transpose row
 
+// Threads of a chunked one-slot CTA at most (K <= 10240): bounding them lets the compiler keep that kernel within 96
+// registers, four CTAs per SM at K = 5120, like the plain kernel.
+constexpr int kRQ256ChunkedThreads = 320;
+
 struct RQ256Piece {
-  int64_t src0, src1;       // element offsets from the row start of the group's first and second piece
-  uint32_t bytes0, bytes1;  // bytes1 == 0: the group lies in one chunk
+  const __nv_bfloat16* src0;  // row 0's address of the group's first piece (add m * ldx for row m)
+  const __nv_bfloat16* src1;  // and of its second piece, when the group straddles two chunks
+  uint32_t bytes0, bytes1;    // bytes1 == 0: the group lies in one chunk
 };
 
 __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages, bool chunked = false) {
@@ -329,12 +343,14 @@ __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stage
   return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + table + 64;
 }
 
-// CHUNKED selects the chunked-row input (the Ulysses receive layout): each row's copies come from a table of
-// (source offset, bytes) pairs built once per CTA, so the per-row issue costs what the plain walk costs.  Plain rows
-// (x_chunk == K) use the instantiation without it, which compiles to 86 registers: at K = 5120 (160 threads) four
-// CTAs fit an SM, which is what the launch assumes (at most 96).
+// CHUNKED selects the chunked-row input (the Ulysses layouts, in this GPU's memory or gathered from the others'):
+// each row's copies come from a table of (address, bytes) pairs built once per CTA, so the per-row issue costs what
+// the plain walk costs, and x_out may receive each gathered row.  Plain rows (x_chunk == K) use the instantiation
+// without it.  The launch sizes residency from the compiled register count; at K = 5120 (160 threads) both forms
+// stay within 96 (plain 86 with no bound; chunked under its thread bound), so four CTAs fit an SM.
 template <int SLOTS, int ROUNDING, bool CHUNKED>
-__global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantParams p) {
+__global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads : 512, CHUNKED && SLOTS == 1 ? 2 : 0)
+    rotate_quant256_kernel(const RotQuantParams p) {
   extern __shared__ __align__(1024) uint8_t rq2_smem_raw[];
   const int K = p.K;
   const int ngroups = K / 256;
@@ -362,16 +378,17 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
     // one bulk copy per group into its padded slot (two when the group straddles a chunk of the input layout);
     // all complete on the stage's barrier
     mbar_arrive_expect_tx(&bars[stage], row_bytes);
-    const __nv_bfloat16* src = p.x + static_cast<int64_t>(m) * p.ldx;
+    const int64_t roff = static_cast<int64_t>(m) * p.ldx;
     uint8_t* dst = rows + stage * stage_bytes;
     if constexpr (!CHUNKED) {
+      const __nv_bfloat16* src = p.x + roff;
       for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlotBytes, src + g * 256, 512, &bars[stage]);
     } else {
 #pragma unroll 1
       for (int g = 0; g < ngroups; ++g) {
         const RQ256Piece pc = pieces[g];
-        bulk_load(dst + g * kSlotBytes, src + pc.src0, pc.bytes0, &bars[stage]);
-        if (pc.bytes1) bulk_load(dst + g * kSlotBytes + pc.bytes0, src + pc.src1, pc.bytes1, &bars[stage]);
+        bulk_load(dst + g * kSlotBytes, pc.src0 + roff, pc.bytes0, &bars[stage]);
+        if (pc.bytes1) bulk_load(dst + g * kSlotBytes + pc.bytes0, pc.src1 + roff, pc.bytes1, &bars[stage]);
       }
     }
   };
@@ -387,8 +404,8 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
         const int c = c0 - j * p.x_chunk;
         const int first = p.x_chunk - c < 256 ? p.x_chunk - c : 256;
         RQ256Piece pc;
-        pc.src0 = j * p.x_chunk_stride + c;
-        pc.src1 = (j + 1) * p.x_chunk_stride;
+        pc.src0 = select_chunk(p.xs, j) + c;
+        pc.src1 = first < 256 ? select_chunk(p.xs, j + 1) : nullptr;
         pc.bytes0 = static_cast<uint32_t>(first) * 2;
         pc.bytes1 = static_cast<uint32_t>(256 - first) * 2;
         pieces[g] = pc;
@@ -410,6 +427,15 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
     volatile int never = 0;
     const bool arrived = mbar_wait_bounded(&bars[st], (it / stages) & 1, p.wait_limit_ns, &never);
     const uint8_t* xr = rows + st * stage_bytes;
+    if constexpr (CHUNKED) {
+      // the gathered row, as it landed: the first thread of each group's team stores that group's slot
+      if (tt == 0 && p.x_out && arrived) {
+#pragma unroll 1
+        for (int g = tid >> 3; g < ngroups; g += nthr >> 3)
+          bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out + g * 256, xr + g * kSlotBytes, 512);
+        bulk_commit_group();
+      }
+    }
 
     float y[SLOTS][32];
     float amax = 0.0f;
@@ -502,11 +528,17 @@ __global__ void __launch_bounds__(512) rotate_quant256_kernel(const RotQuantPara
       }
     }
     if (tid == 0) p.s[m] = scale;
+    if constexpr (CHUNKED) {
+      if (tt == 0 && p.x_out) bulk_wait_group_read<0>();  // the row stores have read this buffer
+    }
     __syncthreads();
     if (tid == 0) {
       const int m_next = m + stages * gridDim.x;
       if (m_next < p.M) issue_row(st, m_next);
     }
+  }
+  if constexpr (CHUNKED) {
+    if (tt == 0 && p.x_out) bulk_wait_group_all();
   }
   if (aborted && tid == 0) {
     volatile int never = 0;

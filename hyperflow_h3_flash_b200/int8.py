@@ -207,6 +207,37 @@ class Int8RotLinear(nn.Module):
         return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
                                       up=self.up.weight if self.rank else None, out_chunks=out_chunks)
 
+    def forward_scatter(self, x: Tensor, out_ptrs: list[int], out_ld: int) -> None:
+        """The layer with its output written as column chunks to device addresses (CUDA only): chunk j of each row
+        to ``out_ptrs[j]`` (``[M, out_ld]`` rows) -- the seq -> head exchange done by the GEMM, when the addresses are
+        the other GPUs' receive buffers."""
+        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
+        if not x2.is_cuda:
+            raise ValueError("forward_scatter runs on CUDA tensors only")
+        kernels = _kernels()
+        if x2.shape[0] >= _MIN_KERNEL_ROWS:
+            xq, sx = self._quantize(x, x2, kernels)
+        else:
+            Int8RotLinear._last_input.clear()
+            self._lowrank_hit = None
+            xq, sx = kernels.rotate_quant_torch_rounding(x2, self.group)
+        xa = self._lowrank_input(x2, kernels) if self.rank else None
+        kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
+                               up=self.up.weight if self.rank else None, out_ptrs=out_ptrs, out_ld=out_ld)
+
+    def forward_gather(self, x_ptrs: list[int], rows: int, ldx: int, device: torch.device) -> Tensor:
+        """The layer on rows gathered from column chunks at device addresses (CUDA only): row m is the concatenation
+        over j of row m of ``[rows, ldx]`` at ``x_ptrs[j]`` -- the head -> seq exchange done by the rotate kernel's
+        row copies, when the addresses are the other GPUs' buffers.  Returns ``[rows, out_features]``."""
+        kernels = _kernels()
+        Int8RotLinear._last_input.clear()
+        self._lowrank_hit = None
+        rounding = _lib.ROUND_KERNEL if rows >= _MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+        xq, sx, xg = kernels.rotate_quant_gather(x_ptrs, ldx, rows, self.in_features, self.group, device, rounding)
+        xa = kernels.lowrank_down(xg, self.down.weight) if self.rank else None
+        return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
+                                      up=self.up.weight if self.rank else None)
+
     def _forward_torch(self, x2: Tensor, rot: Tensor) -> Tensor:
         """The reference's torch path (int8.py:173-179): the rotation is rounded to bf16 and the codes divide by
         the scale. Used for CPU tensors only."""
@@ -312,6 +343,23 @@ def lowrank_down_packed(xp: Tensor, down: Tensor) -> Tensor:
     return xa if ld == r else xa[:, :r]
 
 
+def rotate_quant_gather(x_ptrs: list[int], ldx: int, M: int, K: int, group: int, device: torch.device,
+                        rounding: int = _lib.ROUND_KERNEL) -> tuple[Tensor, Tensor, Tensor]:
+    """``rotate_quant`` of rows gathered from column chunks at device addresses (possibly other GPUs' memory): row m
+    is the concatenation over j of row m of ``[M, ldx]`` at ``x_ptrs[j]`` (``K / len(x_ptrs)`` columns each).  Also
+    returns the gathered bf16 rows ``[M, K]`` (what the low-rank down projection reads)."""
+    n = len(x_ptrs)
+    q = torch.empty(M, K, dtype=torch.int8, device=device)
+    s = torch.empty(M, dtype=torch.float32, device=device)
+    x = torch.empty(M, K, dtype=torch.bfloat16, device=device)
+    ptrs = (ctypes.c_void_p * n)(*x_ptrs)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    rc = _lib.lib().convrot_rotate_quant_gather(ptrs, n, ldx, M, K, group, rounding, _ptr(q), K, _ptr(s), _ptr(x), K,
+                                                stream)
+    _lib.check(rc, "convrot_rotate_quant_gather")
+    return q, s, x
+
+
 def rotate_quant_torch_rounding(x: Tensor, group: int) -> tuple[Tensor, Tensor]:
     """``rotate_quant`` with the reference torch path's rounding (bf16 rotation, division): int8.py:175-178."""
     return rotate_quant(x, group, _lib.ROUND_TORCH)
@@ -337,10 +385,13 @@ def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
 
 
 def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor | None = None,
-                   xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None) -> Tensor:
+                   xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None,
+                   out_ptrs: list[int] | None = None, out_ld: int | None = None) -> Tensor | None:
     """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
 
-    ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout)."""
+    ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout).  ``out_ptrs`` (device
+    addresses, possibly in other GPUs' memory) writes column chunk j as ``[M, out_ld]`` rows at ``out_ptrs[j]`` and
+    returns None: the Ulysses exchange done by the GEMM's stores."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -370,6 +421,17 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         lr = -(-r // 8) * 8
         xa = _pad_cols(xa.to(torch.bfloat16), lr)
         up = _pad_cols(up.to(torch.bfloat16).contiguous(), lr)
+    if out_ptrs is not None:
+        n = len(out_ptrs)
+        if n < 2 or N % n or out_ld is None:
+            raise ValueError(f"N = {N} does not split into {n} chunks, or out_ld is missing")
+        ptrs = (ctypes.c_void_p * n)(*out_ptrs)
+        rc = _lib.lib().convrot_gemm_scatter(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                             _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                             up.stride(0) if up is not None else 0, r, M, N, Kp, ptrs, n, out_ld,
+                                             _stream(a))
+        _lib.check(rc, "convrot_gemm_scatter")
+        return None
     if out_chunks:
         if N % out_chunks:
             raise ValueError(f"N = {N} does not split into {out_chunks} chunks")
@@ -425,6 +487,7 @@ def _kernels() -> SimpleNamespace:
         int8_mm_acc=int8_mm_acc,
         rotate_quant_packed=rotate_quant_packed,
         lowrank_down_packed=lowrank_down_packed,
+        rotate_quant_gather=rotate_quant_gather,
     )
 
 

@@ -8,9 +8,13 @@ Here it is written directly on ``torch.distributed.all_to_all_single`` (NCCL ove
 * around attention, ``seq_to_head`` turns ``[M/P, H, D]`` (local tokens, all heads) into ``[M, H/P, D]`` (all tokens,
   local heads) and ``head_to_seq`` is its inverse.  The head count must be divisible by ``P``
   (distributed.py:68-71).
+* ``PeerExchange`` does the same exchange without a collective: the producing GEMM stores into the other GPUs'
+  receive buffers and the consuming rotate kernel reads from them, ordered by epoch flags.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -62,20 +66,162 @@ def head_to_seq(t: Tensor, group=None) -> Tensor:
     return recv.transpose(0, 1).reshape(m, P * hp * d)
 
 
+class PeerExchange:
+    """The Ulysses exchange over peer memory: this rank's receive buffers, mapped by every rank of the group.
+
+    The buffers live in this GPU's memory; every other rank maps them through CUDA IPC (one process per GPU), so
+    the q/k/v GEMMs of rank i store column block j of their outputs straight into rank j's receive buffer, slot i
+    (``convrot_gemm_scatter``), and the out projection's rotate kernel of rank i reads block i of every rank's
+    attention output straight from that rank's memory (``convrot_rotate_quant_gather``).  No copy, no collective
+    library: the bytes cross NVLink inside the kernels that produce and consume them.
+
+    Ordering is two epoch flags per step (``convrot_peer_signal`` / ``convrot_peer_wait``, release/acquire at
+    system scope, bounded waits):
+
+    * ARRIVED -- rank i has written its q/k/v blocks into every rank.  Rank j waits for all ranks before attention.
+    * READY   -- rank j's attention output is complete.  Rank i waits for all ranks before gathering.
+
+    Those two also cover reuse across steps: rank i writes rank j's receive buffers of step s+1 only after READY(s)
+    from rank j (so j's attention of step s is done reading them), and rank j overwrites its attention output of
+    step s+1 only after ARRIVED(s+1) from rank i, which rank i signals after its gather of step s.
+
+    Layout of each rank's buffer: 4 KiB of flags (phase p, source rank i at word ``8 p + i``), then the receive
+    buffers q, k, v and the attention output, each ``[P, rows, width / P]`` bf16 (block i: rank i's tokens).
+    """
+
+    ARRIVED, READY = 0, 1
+    _NAMES = ("q", "k", "v", "out")
+    _FLAG_BYTES = 4096
+
+    def __init__(self, rows: int, width: int, heads: int, group=None, device: torch.device | None = None):
+        from . import _lib
+
+        self._lib = _lib
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.P > 8 or heads % self.P or width % heads or (width // self.P) % 128:
+            raise ValueError(f"{heads} heads of width {width} cannot be exchanged over {self.P} ranks")
+        self.rows, self.width, self.heads = rows, width, heads
+        self.W = width // self.P
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self._tensor_bytes = self.P * rows * self.W * 2
+        self.buf = torch.zeros(self._FLAG_BYTES + len(self._NAMES) * self._tensor_bytes, dtype=torch.uint8,
+                               device=self.device)
+        L = _lib.lib()
+        handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        offset = ctypes.c_int64(0)
+        _lib.check(L.convrot_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(offset)),
+                   "convrot_ipc_handle")
+        everyone: list = [None] * self.P
+        dist.all_gather_object(everyone, (handle.raw, offset.value), group=group)
+        self._opened: list[int] = []
+        self.base: list[int] = []
+        try:
+            for j, (h, off) in enumerate(everyone):
+                if j == self.rank:
+                    self.base.append(self.buf.data_ptr())
+                    continue
+                mapped = ctypes.c_void_p(0)
+                _lib.check(L.convrot_ipc_open(ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES),
+                                              ctypes.byref(mapped)), "convrot_ipc_open")
+                self._opened.append(mapped.value)
+                self.base.append(mapped.value + off)
+        except Exception:
+            self._unmap()
+            raise
+        self.epoch = 0
+        self.kernel_launches = 0
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+
+    def _offset(self, name: str) -> int:
+        return self._FLAG_BYTES + self._NAMES.index(name) * self._tensor_bytes
+
+    def recv(self, name: str) -> Tensor:
+        """This rank's buffer ``name`` as ``[P, rows, W]`` bf16 (block i: the tokens of rank i)."""
+        o = self._offset(name)
+        return self.buf[o : o + self._tensor_bytes].view(torch.bfloat16).view(self.P, self.rows, self.W)
+
+    def block_ptrs(self, name: str) -> list[int]:
+        """Address of block ``rank`` of buffer ``name`` on every rank: where this rank's q/k/v column block j goes
+        (rank j's heads), and where its out projection reads rank j's attention output for its own tokens."""
+        o = self._offset(name) + self.rank * self.rows * self.W * 2
+        return [b + o for b in self.base]
+
+    def step(self) -> None:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+
+    def signal(self, phase: int) -> None:
+        slots = (ctypes.c_void_p * self.P)(*[b + 4 * (8 * phase + self.rank) for b in self.base])
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        self._lib.check(self._lib.lib().convrot_peer_signal(slots, self.P, self.epoch, stream), "convrot_peer_signal")
+        self.kernel_launches += 1
+
+    def wait(self, phase: int) -> None:
+        flags = ctypes.c_void_p(self.buf.data_ptr() + 4 * 8 * phase)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        self._lib.check(self._lib.lib().convrot_peer_wait(flags, self.P, self.epoch, stream), "convrot_peer_wait")
+        self.kernel_launches += 1
+
+    def _unmap(self) -> None:
+        L = self._lib.lib()
+        for mapped in self._opened:
+            L.convrot_ipc_close(ctypes.c_void_p(mapped))
+        self._opened = []
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buffers; every rank calls it, after its last use of the exchange."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # nobody touches a peer's buffer any more
+        self._unmap()
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more: it may be freed
+        self.base = []
+        self.buf = None
+
+
+def attention_block_peer(x: Tensor, to_q, to_k, to_v, to_out, exchange: PeerExchange, attention=None) -> Tensor:
+    """``attention_block_linears`` with the exchange fused into the kernels over peer memory (see PeerExchange)."""
+    ex = exchange
+    m = x.reshape(-1, x.shape[-1]).shape[0]
+    if m != ex.rows or to_q.out_features != ex.width:
+        raise ValueError(f"exchange is for {ex.rows} x {ex.width}, got {m} x {to_q.out_features}")
+    P, d = ex.P, ex.width // ex.heads
+    ex.step()
+    for name, layer in zip("qkv", (to_q, to_k, to_v)):
+        layer.forward_scatter(x, ex.block_ptrs(name), ex.W)
+    ex.signal(ex.ARRIVED)
+    ex.wait(ex.ARRIVED)
+    if attention is None:
+        source = "v"  # identity attention: the output is v as received
+    else:
+        qh, kh, vh = (ex.recv(n).view(P * m, ex.heads // P, d) for n in "qkv")
+        ex.recv("out").copy_(attention(qh, kh, vh).reshape(P, m, ex.W))
+        source = "out"
+    ex.signal(ex.READY)
+    ex.wait(ex.READY)
+    return to_out.forward_gather(ex.block_ptrs(source), m, ex.W, x.device)
+
+
 def _packed_capable(x: Tensor, layers) -> bool:
     return x.is_cuda and all(hasattr(layer, "forward_packed") for layer in layers)
 
 
-def attention_block_linears(x: Tensor, to_q, to_k, to_v, to_out, heads: int, attention=None, group=None) -> Tensor:
+def attention_block_linears(x: Tensor, to_q, to_k, to_v, to_out, heads: int, attention=None, group=None,
+                            exchange: PeerExchange | None = None) -> Tensor:
     """One attention block's linears on this rank's tokens: q/k/v (sharing one quantisation -- and one low-rank
     projection, see ``int8.share_lowrank`` -- when the layers have ``keep_input``), the seq->head all-to-all,
     ``attention`` (identity -> v when None), head->seq, and ``to_out``.
 
-    With convrot layers on CUDA and more than one rank, the q/k/v GEMMs write their outputs straight into the
-    all-to-all send layout ``[P, M/P, heads/P * D]`` and ``to_out`` reads the receive layout in place, so no pack
-    or unpack copy surrounds the collectives; each q/k/v all-to-all is issued as soon as its GEMM is queued and
-    overlaps the next GEMM."""
+    With convrot layers on CUDA and more than one rank:
+
+    * given an ``exchange`` (``PeerExchange``), the all-to-alls are fused into the kernels over peer memory;
+    * otherwise the q/k/v GEMMs write their outputs straight into the NCCL all-to-all send layout
+      ``[P, M/P, heads/P * D]`` and ``to_out`` reads the receive layout in place, so no pack or unpack copy surrounds
+      the collectives; each q/k/v all-to-all is issued as soon as its GEMM is queued and overlaps the next GEMM."""
     P = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+    if exchange is not None and P > 1:
+        return attention_block_peer(x, to_q, to_k, to_v, to_out, exchange, attention)
     if P == 1 or not _packed_capable(x, (to_q, to_k, to_v, to_out)):
         q, k, v = to_q(x), to_k(x), to_v(x)
         qh, kh, vh = seq_to_head(q, heads, group), seq_to_head(k, heads, group), seq_to_head(v, heads, group)

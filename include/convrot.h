@@ -117,6 +117,41 @@ int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* l
                                 int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
 
 /*
+ * The Ulysses exchange fused into the kernels, over peer memory (no counterpart in the reference, whose all-to-all
+ * is diffusers' NCCL call; call site distributed.py:88-96).  One process per GPU; every rank maps the others'
+ * exchange buffers (convrot_ipc_*), so a chunk pointer below may name another GPU's memory.  At most 8 chunks.
+ *
+ * convrot_gemm_scatter        as convrot_gemm, writing output column chunk j (N / n_chunks columns, a multiple of
+ *                             32) as [M, ldy] rows at y_chunks[j]: the seq -> head all-to-all done by the epilogue's
+ *                             stores.  y_chunks is a host array of device pointers.
+ * convrot_rotate_quant_gather as convrot_rotate_quant, reading row m as the concatenation over j of row m of
+ *                             x_chunks[j] ([M, ldx] rows of K / n_chunks columns, a multiple of 128): the head ->
+ *                             seq all-to-all done by the kernel's row copies.  x_out (optional, bf16 [M, ld_out])
+ *                             receives each gathered row for the low-rank down projection.
+ * convrot_ipc_handle          64-byte CUDA IPC handle of the allocation holding ptr, and ptr's offset in it.
+ * convrot_ipc_open            maps another process's allocation (base address; add the offset); _close unmaps it.
+ * convrot_peer_signal         stores `epoch` to each of the n flags slots[j] (host array of device pointers, usually
+ *                             this rank's slot in rank j's flags) with release semantics at system scope, after the
+ *                             work queued before it on the stream.
+ * convrot_peer_wait           holds the stream until each of the n flags at `flags` has reached `epoch` (acquire at
+ *                             system scope; compared modulo 2^32).  Bounded by the wait limit: on expiry the device
+ *                             error word reads CONVROT_ERR_TIMEOUT (convrot_poll_error) and the stream continues.
+ */
+#define CONVROT_IPC_HANDLE_BYTES 64
+int convrot_gemm_scatter(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                         const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                         int64_t M, int64_t N, int64_t K, void* const* y_chunks, int n_chunks, int64_t ldy,
+                         void* stream);
+int convrot_rotate_quant_gather(const void* const* x_chunks, int n_chunks, int64_t ldx, int64_t M, int64_t K,
+                                int group, int rounding, int8_t* q_out, int64_t ldq, float* s_out, void* x_out,
+                                int64_t ld_out, void* stream);
+int convrot_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+int convrot_ipc_open(const void* handle, void** base_out);
+int convrot_ipc_close(void* base);
+int convrot_peer_signal(uint32_t* const* slots, int n, uint32_t epoch, void* stream);
+int convrot_peer_wait(const uint32_t* flags, int n, uint32_t epoch, void* stream);
+
+/*
  * Workspace for convrot_linear: q (int8 [M, K]), s (fp32 [M]) and xa (bf16 [M, r]), each 256-byte aligned.
  */
 size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r);

@@ -412,3 +412,84 @@ def test_layer_packed_forms_equal_the_plain_forward(M, K, N, r, P):
     assert torch.equal(layer.forward_packed(pack(x, P)), ref)
     with pytest.raises(ValueError):
         layer.forward_packed(x)
+
+
+@pytest.mark.parametrize("M,N,K,r,P", [(333, 5120, 5120, 32, 8), (4096, 2048, 1024, 0, 2), (40, 1536, 512, 64, 4)])
+def test_scatter_gemm_writes_each_chunk_at_its_address(M, N, K, r, P, gemm_mode):
+    """convrot_gemm_scatter with P separate buffers gives the packed output's blocks, bit for bit."""
+    x = synthetic.activations(M, K, seed=61).to(DEV)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256).to(DEV)
+    q, s = I.rotate_quant(x, 256)
+    xa = I.lowrank_down(x, w.down) if r else None
+    up = w.up if r else None
+    packed = I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=up, out_chunks=P)
+    W = N // P
+    ld = W + 64  # rows of each destination further apart than the chunk: the pitch is honoured
+    dests = [torch.full((M, ld), float("nan"), dtype=torch.bfloat16, device=DEV) for _ in range(P)]
+    assert I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=up,
+                            out_ptrs=[t.data_ptr() for t in dests], out_ld=ld) is None
+    for j in range(P):
+        assert torch.equal(dests[j][:, :W], packed[j])
+        assert torch.isnan(dests[j][:, W:].float()).all()  # nothing written past the chunk
+
+
+@pytest.mark.parametrize("M,K,P,group", [(333, 5120, 8, 256), (1000, 4096, 2, 256), (64, 1024, 4, 64),
+                                         (8, 5120, 8, 256)])
+def test_gather_rotate_reads_rows_from_separate_chunks(M, K, P, group, rotate_variant):
+    """convrot_rotate_quant_gather over P separate buffers equals rotate_quant of the plain rows; x_out is x."""
+    x = synthetic.activations(M, K, seed=62).to(DEV)
+    W = K // P
+    ld = W + 128
+    chunks = []
+    for j in range(P):
+        t = torch.zeros(M, ld, dtype=torch.bfloat16, device=DEV)
+        t[:, :W] = x[:, j * W:(j + 1) * W]
+        chunks.append(t)
+    rounding = _lib.ROUND_KERNEL if M >= I._MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+    q, s = I.rotate_quant(x, group) if rounding == _lib.ROUND_KERNEL else I.rotate_quant_torch_rounding(x, group)
+    qg, sg, xg = I.rotate_quant_gather([t.data_ptr() for t in chunks], ld, M, K, group, torch.device(DEV), rounding)
+    assert torch.equal(q, qg) and torch.equal(s, sg)
+    assert torch.equal(xg, x)
+
+
+def test_layer_scatter_and_gather_forms_equal_the_plain_forward():
+    """Int8RotLinear.forward_scatter / forward_gather on local buffers reproduce forward bit for bit."""
+    K, N, r, M, P = 2048, 1024, 32, 300, 4
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256)
+    layer = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+    synthetic.load_into(layer, w)
+    layer = layer.to(DEV)
+    x = synthetic.activations(M, K, seed=63).to(DEV)
+    ref = layer(x)
+    outs = [torch.empty(M, N // P, dtype=torch.bfloat16, device=DEV) for _ in range(P)]
+    layer.forward_scatter(x, [t.data_ptr() for t in outs], N // P)
+    assert torch.equal(torch.cat(outs, dim=1), ref)
+    chunks = [x[:, j * (K // P):(j + 1) * (K // P)].contiguous() for j in range(P)]
+    assert torch.equal(layer.forward_gather([t.data_ptr() for t in chunks], M, K // P, x.device), ref)
+
+
+def test_peer_wait_gives_up_at_its_limit_and_the_stream_goes_on():
+    """A wait on a flag that nothing sets ends at the wait limit with CONVROT_ERR_TIMEOUT on the next poll; the
+    stream is usable afterwards.  A flag that is set (here by this GPU's own signal kernel) passes."""
+    import ctypes
+
+    L = _lib.lib()
+    flags = torch.zeros(8, dtype=torch.int32, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P_ = ctypes.c_void_p
+    L.convrot_set_wait_limit_ns(50_000_000)  # 50 ms
+    try:
+        _lib.check(L.convrot_peer_wait(P_(flags.data_ptr()), 2, 1, stream), "wait")
+        torch.cuda.synchronize()
+        assert L.convrot_poll_error(None) == _lib.ERR_TIMEOUT
+        slots = (ctypes.c_void_p * 2)(flags.data_ptr(), flags.data_ptr() + 4)
+        _lib.check(L.convrot_peer_signal(slots, 2, 7, stream), "signal")
+        _lib.check(L.convrot_peer_wait(P_(flags.data_ptr()), 2, 7, stream), "wait")
+        _lib.check(L.convrot_peer_wait(P_(flags.data_ptr()), 2, 5, stream), "wait")  # already past: passes
+        torch.cuda.synchronize()
+        assert L.convrot_poll_error(None) == 0
+        assert flags[:2].tolist() == [7, 7] and flags[2:].abs().sum().item() == 0
+    finally:
+        L.convrot_set_wait_limit_ns(2_000_000_000)
+    assert L.convrot_peer_signal(None, 2, 1, stream) == _lib.ERR_ARG
+    assert L.convrot_peer_wait(None, 2, 1, stream) == _lib.ERR_ARG
