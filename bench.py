@@ -26,8 +26,8 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
+import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -59,56 +59,64 @@ def parse() -> argparse.Namespace:
 
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms during the timed region (read-only queries)."""
+    """SM clock and throttle reasons sampled every 5 ms during the timed region, through NVML (read-only queries;
+    nvidia-smi's own fields: clocks.sm, clocks.max.sm, clocks_event_reasons.*).  A background thread samples from
+    before the region starts (the first sample is taken before __enter__ returns) until it ends."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_S = 0.005
+    # NVML clocks-event-reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self, nvml, handle):
+        while True:
+            try:
+                mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                self.samples.append((float(mhz), int(reasons)))
+            except Exception:  # noqa: BLE001 - a failed read is a missing sample, not an error of the bench
+                pass
+            if self._stop.wait(self.PERIOD_S):
+                return
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml as nvml
+
+            nvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.index]) if visible else self.index
+            handle = nvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._run, args=(nvml, handle), daemon=True)
+            self._thread.start()
+            deadline = time.time() + 2.0
+            while not self.samples and time.time() < deadline:
+                time.sleep(0.001)
+        except Exception:  # noqa: BLE001 - no NVML: the line reports no clock samples
+            self._thread = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if self._thread is not None:
+            time.sleep(2 * self.PERIOD_S)
+            self._stop.set()
+            self._thread.join(timeout=5)
         return False
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
+        sm = [mhz for mhz, _ in self.samples]
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        mx = self.max_mhz
         loaded = [v for v in sm if mx and v > 0.5 * mx] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(sm), "source": "NVML, every 5 ms during the timed region"}
 
 
 # --------------------------------------------------------------------------------------------------- CPU arm
