@@ -63,13 +63,15 @@ class ClockSampler:
     nvidia-smi's own fields: clocks.sm, clocks.max.sm, clocks_event_reasons.*).  A background thread samples from
     before the region starts (the first sample is taken before __enter__ returns) until it ends."""
 
-    PERIOD_S = 0.005
+    PERIOD_S = float(os.environ.get("HF_CLOCK_PERIOD_MS", "5")) / 1000.0
     # NVML clocks-event-reason bits (nvml.h: nvmlClocksEventReason*)
-    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+    REASONS = {"gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+               "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100}
 
     def __init__(self, index: int):
         self.index = index
-        self.samples: list[tuple[float, int]] = []
+        self.samples: list[tuple[float, int, float]] = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
@@ -79,7 +81,8 @@ class ClockSampler:
             try:
                 mhz = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
                 reasons = nvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                self.samples.append((float(mhz), int(reasons)))
+                watts = nvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                self.samples.append((float(mhz), int(reasons), watts))
             except Exception:  # noqa: BLE001 - a failed read is a missing sample, not an error of the bench
                 pass
             if self._stop.wait(self.PERIOD_S):
@@ -111,12 +114,14 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
-        sm = [mhz for mhz, _ in self.samples]
-        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+        sm = [mhz for mhz, _, _ in self.samples]
+        reasons = sorted(name for name, bit in self.REASONS.items() if any(r & bit for _, r, _ in self.samples))
+        watts = [w for _, _, w in self.samples]
         mx = self.max_mhz
         loaded = [v for v in sm if mx and v > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(sm), "source": "NVML, every 5 ms during the timed region"}
+                "power_w": statistics.median(watts) if watts else None, "samples": len(sm),
+                "source": f"NVML, every {self.PERIOD_S * 1000:g} ms during the timed region"}
 
 
 # --------------------------------------------------------------------------------------------------- CPU arm
@@ -516,6 +521,32 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     out["block_set_cfg3"] = {"config": "config 3: M=32760, r=64, QKV 5120->15360, out 5120->5120, "
                                        "FFN-up 5120->27648, FFN-down 13824->5120 (bias, low-rank)",
                              "ms": ms, "tops": ops / (ms * 1e-3) / 1e12}
+
+    # the same block with the feed-forward's real dataflow: FFN-down reads the SwiGLU of FFN-up's output, either
+    # unfused (projection [M, 27648] -> a * silu(g) in torch -> down) or fused into the FFN-up epilogue
+    from hyperflow_h3_flash_b200 import ffn
+
+    swiglu_up = ffn.SwiGLUInt8(layers["ffn_up"])
+
+    def chain_unfused():
+        return layers["ffn_down"](ffn.swiglu_reference(layers["ffn_up"](xb)))
+
+    def chain_fused():
+        return layers["ffn_down"](swiglu_up(xb))
+
+    def block_fused():
+        layers["qkv"](xb)
+        layers["out"](xb)
+        chain_fused()
+
+    ms_unfused = timed(chain_unfused, max(3, args.steps // 2))
+    ms_fused = timed(chain_fused, max(3, args.steps // 2))
+    ms_block = timed(block_fused, max(3, args.steps // 2))
+    out["ffn_chain_cfg3"] = {"config": "M=32760: FFN-up 5120->27648 (r=64, bias) -> a*silu(g) -> FFN-down "
+                                       "13824->5120 (r=64, bias)",
+                             "ms_unfused": ms_unfused, "ms_fused_swiglu": ms_fused}
+    out["block_set_cfg3_swiglu"] = {"config": "config 3 with FFN-down reading the fused SwiGLU of FFN-up",
+                                    "ms": ms_block, "tops": ops / (ms_block * 1e-3) / 1e12}
     return out
 
 

@@ -246,9 +246,11 @@ using Cfg2LR64 = Gemm2Cfg<5, 128, 1>;
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
             int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream,
-            void* const* chunks = nullptr, int n_chunks = 1) {
+            void* const* chunks = nullptr, int n_chunks = 1, bool swiglu = false) {
   if (n_chunks < 1 || n_chunks > kMaxChunks || (n_chunks > 1 && !chunks)) return CONVROT_ERR_ARG;
-  int64_t out_chunk = N;
+  if (swiglu && (raw || n_chunks > 1)) return CONVROT_ERR_ARG;
+  if (swiglu && N % 64) return CONVROT_ERR_SHAPE;
+  int64_t out_chunk = swiglu ? N / 2 : N;
   if (n_chunks > 1) {
     if (raw || N % n_chunks || (N / n_chunks) % 32) return CONVROT_ERR_SHAPE;
     out_chunk = N / n_chunks;
@@ -295,6 +297,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
     if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, b_rows, lr_atom / 2))) return rc;
   }
   GemmParams p;
+  memset(&p, 0, sizeof(p));
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -305,6 +308,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   for (int j = 0; j < kMaxChunks; ++j) p.out_chunks[j] = j < n_chunks ? (n_chunks > 1 ? chunks[j] : out) : nullptr;
   p.ldo = ldo;
   p.out_chunk = static_cast<int>(out_chunk);
+  p.swiglu = swiglu ? 1 : 0;
   p.a_chunk = static_cast<int>(K);
   p.r = has_lr ? static_cast<int>(r) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
@@ -626,6 +630,13 @@ int convrot_gemm_packed(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
   for (int j = 0; j < n; ++j) chunks[j] = static_cast<uint8_t*>(y) + j * M * chunk_cols * 2;
   return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, chunk_cols, false,
                  static_cast<cudaStream_t>(stream), chunks, n);
+}
+
+int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                        const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                        int64_t M, int64_t N, int64_t K, void* h, int64_t ldh, void* stream) {
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, h, ldh, false,
+                 static_cast<cudaStream_t>(stream), nullptr, 1, true);
 }
 
 int convrot_gemm_scatter(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,

@@ -45,6 +45,8 @@ struct GemmParams {
   void* out_chunks[kMaxChunks];  // bf16 output in column chunks of out_chunk: chunk j is [M, ldo] rows at [j]
   int64_t ldo;          // elements (row pitch of the output, or of each chunk)
   int out_chunk;        // columns per chunk (N for plain rows, out_chunks[0] == out)
+  int swiglu;           // 1: the B rows are a SwiGLU projection interleaved in 32-row blocks (a0 g0 a1 g1 ...);
+                        //    the bf16 output is h = a * silu(g), [M, N / 2]
   int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
   uint64_t wait_limit_ns;
@@ -155,6 +157,31 @@ __device__ __forceinline__ void store_bf16_chunk(__nv_bfloat16* dst, const float
     for (int j = 0; j < 32; ++j)
       if (n + j < N) dst[j] = __float2bfloat16_rn(t[j]);
   }
+}
+
+// SwiGLU over the interleaved projection, one 32-column block at a time (c = the block's first column in the tile):
+// an `a` block (c / 32 even) is kept as bf16 in ya; on the `g` block that follows, t becomes the pair's 32 outputs
+//   h = bf16( float(bf16(a)) * float(bf16( g / (1 + exp(-g)) )) ),  g = float(bf16(t)),
+// the bf16 composition that `a * silu(g)` evaluates on the bf16 outputs of the projection (silu in fp32, each result
+// rounded to bf16; the product of two bf16 values is exact in fp32, so the caller's bf16 store rounds it once).
+// Returns whether t holds outputs to store.
+__device__ __forceinline__ bool swiglu_block(float (&t)[32], int c, uint32_t (&ya)[16]) {
+  if (((c >> 5) & 1) == 0) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
+      ya[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return false;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float a = __uint_as_float((j & 1) ? (ya[j >> 1] & 0xffff0000u) : (ya[j >> 1] << 16));
+    const float g = __bfloat162float(__float2bfloat16_rn(t[j]));
+    const float silu = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+    t[j] = __fmul_rn(a, silu);
+  }
+  return true;
 }
 
 template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
@@ -421,6 +448,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
       if (EPI == EPI_DEQUANT) {
         const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+        const int n_out = p.swiglu ? p.N >> 1 : p.N;
+        uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t v[32];
@@ -434,8 +463,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
-          } else if (row_ok) {
-            store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
+          } else if (!p.swiglu) {
+            if (row_ok) store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
+          } else if (swiglu_block(t, c, ya) && row_ok) {
+            store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n - 32) >> 1), t, (n - 32) >> 1, n_out);
           }
         }
         if (HAS_LR) {
@@ -458,7 +489,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
+            if (!p.swiglu)
+              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
+            else if (swiglu_block(t, c, ya))
+              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n0 + c - 32) >> 1), t, (n0 + c - 32) >> 1, n_out);
           }
         }
       } else if (EPI == EPI_RAW_I32) {

@@ -401,7 +401,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     auto stage_and_store = [&](const float (&t)[32], int m_box, int n_col) {
       // A box wholly right of N has nothing to store; skipping it also keeps jy inside the maps that exist (with
       // one chunk of width N, n_col >= N would name chunk 1).  n_col is warp-uniform.
-      if (n_col >= p.N) return;
+      if (n_col >= (p.swiglu ? p.N >> 1 : p.N)) return;
       uint8_t* box = my_boxes + box_sel * Cfg::kStoreBoxBytes;
       if (lane == 0) bulk_wait_group_read<1>();  // the store that used this box two chunks ago has read it
       __syncwarp();
@@ -442,6 +442,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
       if (EPI == EPI_DEQUANT) {
         const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+        uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t v[32];
@@ -455,8 +456,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
-          } else {
+          } else if (!p.swiglu) {
             stage_and_store(t, m0 + quad * 32, n);  // rows beyond M are clipped by the TMA store
+          } else if (swiglu_block(t, c, ya)) {
+            stage_and_store(t, m0 + quad * 32, (n - 32) >> 1);
           }
         }
         if (HAS_LR) {
@@ -477,7 +480,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            stage_and_store(t, m0 + quad * 32, n0 + c);
+            if (!p.swiglu)
+              stage_and_store(t, m0 + quad * 32, n0 + c);
+            else if (swiglu_block(t, c, ya))
+              stage_and_store(t, m0 + quad * 32, (n0 + c - 32) >> 1);
           }
         }
       } else {  // EPI_RAW_I32

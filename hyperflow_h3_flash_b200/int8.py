@@ -386,12 +386,14 @@ def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
 
 def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor | None = None,
                    xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None,
-                   out_ptrs: list[int] | None = None, out_ld: int | None = None) -> Tensor | None:
+                   out_ptrs: list[int] | None = None, out_ld: int | None = None,
+                   swiglu: bool = False) -> Tensor | None:
     """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
 
     ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout).  ``out_ptrs`` (device
     addresses, possibly in other GPUs' memory) writes column chunk j as ``[M, out_ld]`` rows at ``out_ptrs[j]`` and
-    returns None: the Ulysses exchange done by the GEMM's stores."""
+    returns None: the Ulysses exchange done by the GEMM's stores.  ``swiglu`` treats b (and sb, bias, up) as a gated
+    projection interleaved in 32-row blocks (``ffn.interleave_rows``) and returns ``h = a * silu(g)``, ``[M, N / 2]``."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -421,6 +423,19 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         lr = -(-r // 8) * 8
         xa = _pad_cols(xa.to(torch.bfloat16), lr)
         up = _pad_cols(up.to(torch.bfloat16).contiguous(), lr)
+    if swiglu:
+        if out_ptrs is not None or out_chunks:
+            raise ValueError("swiglu writes one plain [M, N / 2] output")
+        if N % 64:
+            raise ValueError(f"a SwiGLU projection needs N % 64 == 0, got N = {N}")
+        ldh = -(-(N // 2) // 8) * 8
+        h = torch.empty(M, ldh, dtype=torch.bfloat16, device=a.device)
+        rc = _lib.lib().convrot_gemm_swiglu(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                            _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                            up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(h), ldh,
+                                            _stream(a))
+        _lib.check(rc, "convrot_gemm_swiglu")
+        return h if ldh == N // 2 else h[:, : N // 2]
     if out_ptrs is not None:
         n = len(out_ptrs)
         if n < 2 or N % n or out_ld is None:

@@ -117,6 +117,18 @@ int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* l
                                 int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
 
 /*
+ * The FFN's SwiGLU fused into the up projection's epilogue (no counterpart in the reference: diffusers' gated `net[0]`
+ * runs `proj`, then `a, g = y.chunk(2, -1)`, then `a * silu(g)`; call site transformer.py:87-99).  The B operand is
+ * the projection with its rows interleaved in 32-row blocks -- rows [64 j, 64 j + 32) are rows [32 j, 32 j + 32) of
+ * the `a` half and rows [64 j + 32, 64 j + 64) those of the `g` half -- and ws, bias and lr_up are permuted alike.
+ * N is the full projection width (a multiple of 64); h is bf16 [M, N / 2] with leading dimension ldh:
+ *   h = bf16( bf16(a) * bf16( g / (1 + exp(-g)) ) ),  g = bf16(projection output), silu in fp32.
+ */
+int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                        const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                        int64_t M, int64_t N, int64_t K, void* h, int64_t ldh, void* stream);
+
+/*
  * The Ulysses exchange fused into the kernels, over peer memory (no counterpart in the reference, whose all-to-all
  * is diffusers' NCCL call; call site distributed.py:88-96).  One process per GPU; every rank maps the others'
  * exchange buffers (convrot_ipc_*), so a chunk pointer below may name another GPU's memory.  At most 8 chunks.

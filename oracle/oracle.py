@@ -218,6 +218,21 @@ def composite_reference(x_bits, qweight, wscale, group, bias=None, A=None, B=Non
     return f32_to_bf16(y)
 
 
+def swiglu(y_bits: np.ndarray, gate_first: bool = False) -> np.ndarray:
+    """The gated feed-forward activation on a projection's bf16 output, as bf16 bits: ``a, g = y.chunk(2, -1)``
+    (``g, a`` with gate_first), ``h = bf16(a * bf16(silu(g)))``, ``silu(g) = g / (1 + exp(-g))`` in fp32 -- the bf16
+    torch ops of the gated ``net[0]`` that the reference's ChunkedFeedForward runs (transformer.py:87-90; the module
+    itself is diffusers', absent here).  numpy's float32 exp may differ from CUDA's in the last bit, so results can
+    differ from a GPU's by one bf16 ulp where silu lands next to a rounding boundary."""
+    y = bf16_to_f32(y_bits)
+    half = y.shape[-1] // 2
+    a, g = (y[..., half:], y[..., :half]) if gate_first else (y[..., :half], y[..., half:])
+    with np.errstate(over="ignore"):
+        s = (g / (np.float32(1) + np.exp(-g))).astype(np.float32)
+    s = bf16_to_f32(f32_to_bf16(s))
+    return f32_to_bf16((a * s).astype(np.float32))
+
+
 def forward_cpu_port(x_bits: np.ndarray, qweight: np.ndarray, wscale: np.ndarray, group: int,
                      rotation: np.ndarray | None = None) -> np.ndarray:
     """numpy/BLAS port of the reference CPU path ``Int8RotLinear._forward_torch`` (int8.py:173-179).

@@ -1,0 +1,49 @@
+"""The fused SwiGLU projection: host logic on CPU (row interleave, CPU path, oracle restatement)."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from hyperflow_h3_flash_b200 import ffn
+from hyperflow_h3_flash_b200 import int8 as I
+from hyperflow_h3_flash_b200 import synthetic
+from oracle import oracle as O
+
+
+def test_interleave_rows_pairs_32_row_blocks_of_each_half():
+    perm = ffn.interleave_rows(256)
+    assert sorted(perm.tolist()) == list(range(256))
+    assert perm[:32].tolist() == list(range(0, 32)) and perm[32:64].tolist() == list(range(128, 160))
+    assert perm[64:96].tolist() == list(range(32, 64)) and perm[96:128].tolist() == list(range(160, 192))
+    gf = ffn.interleave_rows(256, gate_first=True)
+    assert gf[:32].tolist() == list(range(128, 160)) and gf[32:64].tolist() == list(range(0, 32))
+    try:
+        ffn.interleave_rows(96)
+    except ValueError:
+        pass
+    else:
+        raise AssertionError("a width that is not a multiple of 64 must be refused")
+
+
+def test_cpu_path_is_the_unfused_composition():
+    K, N = 512, 256
+    w = synthetic.linear_weights(K, N, rank=16, bias=True, group=256)
+    proj = I.Int8RotLinear(K, N, 256, bias=True, rank=16)
+    synthetic.load_into(proj, w)
+    fused = ffn.SwiGLUInt8(proj)
+    x = synthetic.activations(24, K, seed=4)
+    y = proj(x)
+    assert torch.equal(fused(x), y[:, :128] * F.silu(y[:, 128:]))
+    assert fused(x).shape == (24, 128)
+
+
+def test_oracle_swiglu_matches_torch_cpu_within_one_ulp():
+    g = torch.Generator().manual_seed(0)
+    y = (torch.randn(64, 512, generator=g) * 4).to(torch.bfloat16)
+    y[0, :8] = torch.tensor([0.0, -0.0, 100.0, -100.0, -90.0, 88.0, 1e-3, -1e-3])
+    ref = ffn.swiglu_reference(y).view(torch.int16).numpy().view(np.uint16)
+    got = O.swiglu(y.view(torch.int16).numpy().view(np.uint16))
+    diff = np.abs(got.astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() >= 0.999

@@ -493,3 +493,41 @@ def test_peer_wait_gives_up_at_its_limit_and_the_stream_goes_on():
         L.convrot_set_wait_limit_ns(2_000_000_000)
     assert L.convrot_peer_signal(None, 2, 1, stream) == _lib.ERR_ARG
     assert L.convrot_peer_wait(None, 2, 1, stream) == _lib.ERR_ARG
+
+
+@pytest.mark.parametrize("M,K,N,r,bias", [(333, 5120, 27648, 64, True), (4096, 1024, 2048, 0, False),
+                                          (17, 512, 1024, 32, True), (8, 2048, 512, 16, True)])
+def test_fused_swiglu_is_bitwise_the_unfused_composition(M, K, N, r, bias, gemm_mode):
+    """SwiGLUInt8 (the projection GEMM writing a * silu(g)) equals the projection followed by the bf16 torch ops
+    on the GPU, and the oracle's restatement of those ops within one bf16 ulp."""
+    from hyperflow_h3_flash_b200 import ffn
+
+    w = synthetic.linear_weights(K, N, rank=r, bias=bias, group=256, seed_offset=7)
+    proj = I.Int8RotLinear(K, N, 256, bias=bias, rank=r)
+    synthetic.load_into(proj, w)
+    proj = proj.to(DEV)
+    fused = ffn.SwiGLUInt8(proj)
+    x = synthetic.activations(M, K, seed=71).to(DEV)
+    y = proj(x)
+    ref = ffn.swiglu_reference(y)
+    h = fused(x)
+    assert h.shape == (M, N // 2)
+    assert torch.equal(h, ref)
+    orc = O.swiglu(bits(y))
+    diff = np.abs(bits(h).astype(np.int32) - orc.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() >= 0.999
+
+
+def test_fused_swiglu_gate_first_and_shape_checks():
+    from hyperflow_h3_flash_b200 import ffn
+
+    K, N = 1024, 512
+    w = synthetic.linear_weights(K, N, rank=0, bias=False, group=256, seed_offset=8)
+    proj = I.Int8RotLinear(K, N, 256)
+    synthetic.load_into(proj, w)
+    proj = proj.to(DEV)
+    x = synthetic.activations(200, K, seed=72).to(DEV)
+    assert torch.equal(ffn.SwiGLUInt8(proj, gate_first=True)(x), ffn.swiglu_reference(proj(x), gate_first=True))
+    q, s = I.rotate_quant(x, 256)
+    with pytest.raises(ValueError):
+        I.convrot_matmul(q, proj.qweight[:480], s, proj.wscale[:480], swiglu=True)  # 480 % 64 != 0
