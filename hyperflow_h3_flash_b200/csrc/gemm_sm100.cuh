@@ -62,6 +62,22 @@ __device__ __forceinline__ T* out_ptr(const GemmParams& p, int row, int n) {
 }
 
 constexpr int kBM = 128;
+
+// Tile order of the persistent GEMMs: groups of kGroupM M blocks, and inside a group the M block varies fastest, then
+// the N block.  The tiles in flight at once (one per CTA or CTA pair) then cover a few M blocks times a few N blocks,
+// so the A rows and B rows they read stay in L2 even when B (the weights: 141 MB for a 5120 -> 27648 projection) is
+// larger than L2.  In plain row-major order every M block would stream all of B from HBM again.
+constexpr int kGroupM = 8;
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int group_tiles = kGroupM * num_n;
+  const int g = tile / group_tiles;
+  const int first = g * kGroupM;
+  const int rows = num_m - first < kGroupM ? num_m - first : kGroupM;
+  const int in = tile - g * group_tiles;
+  mb = first + in % rows;
+  nb = in / rows;
+}
 constexpr int kRowBytes = 128;  // bytes of K per stage row (one SWIZZLE_128B atom)
 
 __host__ __device__ constexpr int tmem_cols_for(int bn) {
@@ -264,8 +280,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t issued_mask = 0, issued_parity = 0;  // last load per stage, for draining after an abort
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / num_n) * kBM;
-        const int n0 = (tile % num_n) * BN;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * kBM;
+        const int n0 = nb * BN;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, limit, abort_flag)) {
             fail();
@@ -407,8 +425,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t loaded_parity = 0;
       int i = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
-        const int m0 = (tile / num_n) * kBM;
-        const int n0 = (tile % num_n) * BN;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * kBM;
+        const int n0 = nb * BN;
         // tile i reuses the operand buffer once the low-rank MMA of tile i-1 (phase i-1 of lr_empty) is done
         if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
           fail();
@@ -435,8 +455,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
       const uint32_t buf = i & 1;
       const uint32_t par = (i >> 1) & 1;
-      const int m0 = (tile / num_n) * kBM;
-      const int n0 = (tile % num_n) * BN;
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * kBM;
+      const int n0 = nb * BN;
       if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
         fail();
         break;

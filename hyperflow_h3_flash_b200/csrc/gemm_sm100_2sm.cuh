@@ -238,8 +238,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
-        const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * Cfg::kBHalf;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kBHalf;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, limit, abort_flag)) {
             fail();
@@ -371,8 +373,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       int i = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
-        const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * Cfg::kBHalf;
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kBHalf;
         if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
           fail();
           ok = false;
@@ -430,8 +434,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
       const uint32_t buf = i & 1;
       const uint32_t par = (i >> 1) & 1;
-      const int m0 = (tile / num_n) * 2 * kBM + static_cast<int>(rank) * kBM;
-      const int n0 = (tile % num_n) * BN;
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int n0 = nb * BN;
       if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
         fail();
         break;
