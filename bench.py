@@ -50,7 +50,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
-    ap.add_argument("--case", choices=["gemm", "gemm_plain", "rotate", "down"], default=None,
+    ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "down"], default=None,
                     help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
     return ap.parse_args()
 
@@ -580,7 +580,16 @@ def run_case(args) -> None:
     w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP).to(dev)
     q, s = I.rotate_quant(x, GROUP)
     xa = I.lowrank_down(x, w.down)
+    if args.case == "gemm_ffn_up":  # config 3's FFN-up with the fused SwiGLU: B (141 MB) is larger than L2
+        from hyperflow_h3_flash_b200 import ffn
+
+        wf = synthetic.linear_weights(K_DIM, 2 * 13824, rank=64, bias=True, group=GROUP, seed_offset=22)
+        perm = ffn.interleave_rows(2 * 13824)
+        wf = synthetic.LinearWeights(wf.qweight[perm], wf.wscale[perm], wf.bias[perm], wf.down, wf.up[perm]).to(dev)
+        xa64 = I.lowrank_down(x, wf.down)
     fns = {
+        "gemm_ffn_up": lambda: I.convrot_matmul(q, wf.qweight, s, wf.wscale, bias=wf.bias, xa=xa64, up=wf.up,
+                                                swiglu=True),
         "gemm": lambda: I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up),
         "gemm_plain": lambda: I.int8_matmul(q, w.qweight, s, w.wscale),
         "rotate": lambda: I.rotate_quant(x, GROUP),

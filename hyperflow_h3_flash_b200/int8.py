@@ -152,7 +152,7 @@ class Int8RotLinear(nn.Module):
         if stored is not None and stored[0] is peers:
             fused = stored[1]
         else:
-            fused = kernels.lowrank_down(x2, torch.cat([layer.down.weight for layer in peers]))
+            fused = kernels.lowrank_down(x2, _stacked_down(peers))
         if self.keep_input:
             Int8RotLinear._last_input["lowrank"] = (peers, fused)
         start = 0
@@ -247,6 +247,18 @@ class Int8RotLinear(nn.Module):
         xq = torch.clamp(torch.round(xr / sx), -127, 127)
         acc = xq @ self.qweight.float().t()
         return (acc * sx * self.wscale[None, :]).to(torch.bfloat16)
+
+
+def _stacked_down(peers: tuple) -> Tensor:
+    """``[down_q; down_k; down_v]`` for layers joined by ``share_lowrank``, built once and rebuilt only when one of
+    the weights is replaced, moved or modified in place (kept on the first layer, keyed by address and version)."""
+    key = tuple((layer.down.weight.data_ptr(), layer.down.weight._version) for layer in peers)
+    cached = getattr(peers[0], "_stacked_down_cache", None)
+    if cached is None or cached[0] != key:
+        with torch.no_grad():
+            cached = (key, torch.cat([layer.down.weight.detach() for layer in peers]))
+        peers[0]._stacked_down_cache = cached
+    return cached[1]
 
 
 def share_lowrank(*layers: Int8RotLinear) -> None:
