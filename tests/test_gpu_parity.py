@@ -166,9 +166,9 @@ def test_lowrank_down_within_one_bf16_ulp(M, K, r):
 
 
 @pytest.mark.parametrize("M,K,N,r,group", [
-    (40, 1024, 256, 16, 256), (333, 4096, 5120, 32, 256), (256, 5120, 512, 64, 256), (17, 512, 300, 48, 16),
-    (130, 2048, 1000, 0, 64),
-])
+    (40, 1024, 256, 16, 256), (333, 4096, 5120, 32, 256), (256, 4096, 5120, 32, 256), (256, 5120, 512, 64, 256),
+    (17, 512, 300, 48, 16), (130, 2048, 1000, 0, 64),
+])  # (256 | 333, 4096 -> 5120, r = 32): config 5
 def test_fused_bias_and_low_rank_within_tolerance(M, K, N, r, group, gemm_mode):
     x = synthetic.activations(M, K, seed=13)
     w = synthetic.linear_weights(K, N, rank=r, bias=True, group=group)
