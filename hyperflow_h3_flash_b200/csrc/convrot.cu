@@ -267,7 +267,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   if (!raw && (!sx || !ws)) return CONVROT_ERR_ARG;
   const bool has_lr = !raw && xa && up && r > 0;
   if (!raw && (xa || up) && !has_lr) return CONVROT_ERR_ARG;
-  if (has_lr && r > 64) return CONVROT_ERR_SHAPE;
+  if (has_lr && r > 256) return CONVROT_ERR_SHAPE;
   if (K % 16 || ldq < K || ldw < K || ldo < out_chunk) return CONVROT_ERR_SHAPE;
   if (ldq % 16 || ldw % 16 || !aligned16(q) || !aligned16(w)) return CONVROT_ERR_ALIGN;
   if (raw ? (ldo % 4 || !aligned16(out)) : (ldo % 8 || !aligned16(out))) return CONVROT_ERR_ALIGN;

@@ -231,6 +231,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  // The low-rank term streams through its operand buffers in rank chunks of LR_ATOMS * LR_ATOM / 2 columns.
+  const int lr_chunks = HAS_LR ? (p.r + LR_ATOMS * (LR_ATOM / 2) - 1) / (LR_ATOMS * (LR_ATOM / 2)) : 0;
   const int nkb = (p.K * (KIND == KIND_I8 ? 1 : 2) + kRowBytes - 1) / kRowBytes;
   constexpr int kKPerStage = KIND == KIND_I8 ? 128 : 64;  // elements
 
@@ -318,42 +320,56 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int pending_lr = -1;  // local tile index whose low-rank MMA is not issued yet
+      int pending_chunk = 0;  // its next rank chunk
+      bool lr_epi_seen = false;  // its epilogue pass 1 is done
       uint32_t lr_full_phase = 0;
       const uint32_t ring_base = smem_u32(ring);
       const uint32_t xa_base = smem_u32(lr_xa);
       const uint32_t up_base = smem_u32(lr_up);
-      // Issues the low-rank MMA of local tile j: D[buf j] += xa_tile . up_tile^T (kind::f16, K = 16 per MMA).
-      auto issue_lr = [&](int j) {
+      // Issues one rank chunk of the low-rank MMA of local tile j: D[buf j] += xa_chunk . up_chunk^T (kind::f16,
+      // K = 16 per MMA); the last chunk also signals the epilogue.
+      auto issue_lr_chunk = [&](int j, bool last) {
         const uint32_t d = tmem_base + (j & 1) * BN;
-        int kstep = 0;
         for (int a = 0; a < LR_ATOMS; ++a) {
-          for (int off = 0; off < LR_ATOM; off += 32, ++kstep) {
+          for (int off = 0; off < LR_ATOM; off += 32) {
             const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
             const uint64_t bd = make_kmajor_desc(up_base + a * BN * LR_ATOM + off, LR_ATOM);
             mma_f16(d, ad, bd, Cfg::kIdescLR, 1u);
           }
         }
-        mma_commit(&lr_done[j & 1]);
+        if (last) mma_commit(&lr_done[j & 1]);
         mma_commit(lr_empty);
       };
-      // Non-blocking: issue the pending low-rank MMA once its epilogue pass 1 and operands are in place.
+      auto lr_step = [&]() {
+        tc_fence_after();
+        const bool last = pending_chunk + 1 == lr_chunks;
+        issue_lr_chunk(pending_lr, last);
+        lr_full_phase ^= 1;
+        if (last)
+          pending_lr = -1;
+        else
+          ++pending_chunk;
+      };
+      // Non-blocking: issue the pending tile's next rank chunk once its epilogue pass 1 and the chunk are in place.
       auto try_lr = [&]() {
         if (!HAS_LR || pending_lr < 0) return;
-        if (!mbar_try_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+        if (!lr_epi_seen) {
+          if (!mbar_try_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+          lr_epi_seen = true;
+        }
         if (!mbar_try_wait(lr_full, lr_full_phase)) return;
-        tc_fence_after();
-        issue_lr(pending_lr);
-        lr_full_phase ^= 1;
-        pending_lr = -1;
+        lr_step();
       };
       auto flush_lr = [&]() -> bool {
-        if (!HAS_LR || pending_lr < 0) return true;
-        if (!mbar_wait_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag)) return false;
-        if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
-        tc_fence_after();
-        issue_lr(pending_lr);
-        lr_full_phase ^= 1;
-        pending_lr = -1;
+        while (HAS_LR && pending_lr >= 0) {
+          if (!lr_epi_seen) {
+            if (!mbar_wait_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
+              return false;
+            lr_epi_seen = true;
+          }
+          if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
+          lr_step();
+        }
         return true;
       };
       int i = 0;
@@ -409,6 +425,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             break;
           }
           pending_lr = i;
+          pending_chunk = 0;
+          lr_epi_seen = false;
         }
       }
       if (ok && !flush_lr()) ok = false;
@@ -423,24 +441,29 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     if (lane == 0) {
       bool loaded = false;
       uint32_t loaded_parity = 0;
-      int i = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+      int u = 0;  // rank chunks loaded so far (all tiles)
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * kBM;
         const int n0 = nb * BN;
-        // tile i reuses the operand buffer once the low-rank MMA of tile i-1 (phase i-1 of lr_empty) is done
-        if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
-          fail();
-          break;
+        for (int c = 0; c < lr_chunks; ++c, ++u) {
+          // load u reuses the operand buffer once the MMA of load u-1 (phase u-1 of lr_empty) is done
+          if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
+          for (int a = 0; a < LR_ATOMS; ++a) {
+            const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
+            tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, x, m0);
+            tma_load_2d(lr_up + a * BN * LR_ATOM, &tmap_up, lr_full, x, n0);
+          }
+          loaded = true;
+          loaded_parity = u & 1;
         }
-        mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
-        for (int a = 0; a < LR_ATOMS; ++a) {
-          tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, a * (LR_ATOM / 2), m0);
-          tma_load_2d(lr_up + a * BN * LR_ATOM, &tmap_up, lr_full, a * (LR_ATOM / 2), n0);
-        }
-        loaded = true;
-        loaded_parity = i & 1;
       }
       if (loaded && *abort_flag) {
         volatile int never = 0;

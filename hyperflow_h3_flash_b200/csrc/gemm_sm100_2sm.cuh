@@ -186,6 +186,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   const int num_m = (p.M + 2 * kBM - 1) / (2 * kBM);
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  // The low-rank term streams through its operand buffers in rank chunks of LR_ATOMS * LR_ATOM / 2 columns.
+  const int lr_chunks = HAS_LR ? (p.r + LR_ATOMS * (LR_ATOM / 2) - 1) / (LR_ATOMS * (LR_ATOM / 2)) : 0;
   const int nkb = (p.K + kRowBytes - 1) / kRowBytes;
 
   if (threadIdx.x == 0) {
@@ -269,7 +271,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     if (lane == 0 && rank == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int pending_lr = -1;
+      int pending_lr = -1;       // local tile index whose low-rank MMA is not issued yet
+      int pending_chunk = 0;     // its next rank chunk
+      bool lr_epi_seen = false;  // both CTAs' epilogue pass 1 is done for it
       uint32_t lr_full_phase = 0;
       const uint32_t ring_base = smem_u32(ring);
       const uint32_t xa_base = smem_u32(lr_xa);
@@ -278,7 +282,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       const uint32_t tfull_self = smem_u32(tmem_full), tfull_peer = mapa_shared(tfull_self, 1);
       const uint32_t lrdone_self = smem_u32(lr_done), lrdone_peer = mapa_shared(lrdone_self, 1);
       const uint32_t lrempty_self = smem_u32(lr_empty), lrempty_peer = mapa_shared(lrempty_self, 1);
-      auto issue_lr = [&](int j) {
+      // One rank chunk of the low-rank MMA of local tile j (both CTAs' halves); the last also signals the epilogues.
+      auto issue_lr_chunk = [&](int j, bool last) {
         const uint32_t d = tmem_base + (j & 1) * BN;
         for (int a = 0; a < LR_ATOMS; ++a) {
           for (int off = 0; off < LR_ATOM; off += 32) {
@@ -287,29 +292,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             mma_f16_pair(d, ad, bd, Cfg::kIdescLR, 1u);
           }
         }
-        mma_commit_pair(lrdone_self + (j & 1) * 8);
-        mma_commit_pair(lrdone_peer + (j & 1) * 8);
+        if (last) {
+          mma_commit_pair(lrdone_self + (j & 1) * 8);
+          mma_commit_pair(lrdone_peer + (j & 1) * 8);
+        }
         mma_commit_pair(lrempty_self);
         mma_commit_pair(lrempty_peer);
       };
+      auto lr_step = [&]() {
+        tc_fence_after();
+        const bool last = pending_chunk + 1 == lr_chunks;
+        issue_lr_chunk(pending_lr, last);
+        lr_full_phase ^= 1;
+        if (last)
+          pending_lr = -1;
+        else
+          ++pending_chunk;
+      };
       auto try_lr = [&]() {
         if (!HAS_LR || pending_lr < 0) return;
-        if (!mbar_try_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+        if (!lr_epi_seen) {
+          if (!mbar_try_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+          lr_epi_seen = true;
+        }
         if (!mbar_try_wait(lr_full, lr_full_phase)) return;
-        tc_fence_after();
-        issue_lr(pending_lr);
-        lr_full_phase ^= 1;
-        pending_lr = -1;
+        lr_step();
       };
       auto flush_lr = [&]() -> bool {
-        if (!HAS_LR || pending_lr < 0) return true;
-        if (!mbar_wait_cluster_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
-          return false;
-        if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
-        tc_fence_after();
-        issue_lr(pending_lr);
-        lr_full_phase ^= 1;
-        pending_lr = -1;
+        while (HAS_LR && pending_lr >= 0) {
+          if (!lr_epi_seen) {
+            if (!mbar_wait_cluster_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
+              return false;
+            lr_epi_seen = true;
+          }
+          if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
+          lr_step();
+        }
         return true;
       };
       int i = 0;
@@ -359,6 +377,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             break;
           }
           pending_lr = i;
+          pending_chunk = 0;
+          lr_epi_seen = false;
         }
       }
       if (ok && !flush_lr()) ok = false;
@@ -370,22 +390,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   } else if (HAS_LR && warp == 6) {
     // ------------------------------------------------------------ TMA producer: low-rank tiles of this CTA
     if (lane == 0) {
-      int i = 0;
+      int u = 0;  // rank chunks loaded so far (all tiles)
       bool ok = true;
-      for (int tile = pair; tile < num_tiles; tile += num_pairs, ++i) {
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kBHalf;
-        if (!mbar_wait_bounded(lr_empty, (i & 1) ^ 1, limit, abort_flag)) {
-          fail();
-          ok = false;
-          break;
-        }
-        if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
-        for (int a = 0; a < LR_ATOMS; ++a) {
-          tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, a * (LR_ATOM / 2), m0);
-          tma_load_2d_pair(lr_up + a * Cfg::kBHalf * LR_ATOM, &tmap_up, leader_lr_full, a * (LR_ATOM / 2), n0);
+        for (int c = 0; c < lr_chunks; ++c, ++u) {
+          // load u reuses the operand buffers once the MMA of load u-1 (phase u-1 of lr_empty) is done
+          if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
+          for (int a = 0; a < LR_ATOMS; ++a) {
+            const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
+            tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x, m0);
+            tma_load_2d_pair(lr_up + a * Cfg::kBHalf * LR_ATOM, &tmap_up, leader_lr_full, x, n0);
+          }
         }
       }
       if (!ok) {

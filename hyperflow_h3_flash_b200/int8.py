@@ -40,8 +40,9 @@ ROTATE_QUANTS = ("dense", "factored")
 #: Inputs with fewer rows reproduce the reference's torch-path rounding (int8.py:41-43, 164).
 _MIN_KERNEL_ROWS = 17
 
-#: Largest low-rank width fused into the GEMM epilogue.
-MAX_FUSED_RANK = 64
+#: Largest low-rank width fused into the GEMM epilogue (streamed through it in chunks of 64; the reference pads
+#: ranks to multiples of 64 at load, transformer.py:45, 205-216).
+MAX_FUSED_RANK = 256
 
 KERNEL_OPTIONS: dict[str, Any] = {"int8_gemm": "auto", "rotate_quant": "dense"}
 
@@ -147,7 +148,7 @@ class Int8RotLinear(nn.Module):
         result lives in the same cache and dies with it."""
         peers = getattr(self, "_lowrank_peers", None)
         stored, self._lowrank_hit = getattr(self, "_lowrank_hit", None), None
-        if not peers:
+        if not peers or sum(layer.rank for layer in peers) > MAX_FUSED_RANK:  # one down GEMM covers 256 outputs
             return kernels.lowrank_down(x2, self.down.weight)
         if stored is not None and stored[0] is peers:
             fused = stored[1]

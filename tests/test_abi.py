@@ -73,7 +73,7 @@ def test_bad_arguments_are_rejected_before_any_device_call(lib):
     p = ctypes.c_void_p(4096)
     assert L.convrot_gemm(p, 72, p, 64, p, p, None, None, 0, None, 0, 0, 4, 8, 64, p, 8, None) == lib.ERR_ALIGN
     assert L.convrot_gemm(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 8, 40, p, 8, None) == lib.ERR_SHAPE
-    assert L.convrot_gemm(p, 64, p, 64, p, p, None, p, 128, p, 128, 128, 4, 8, 64, p, 8, None) == lib.ERR_SHAPE
+    assert L.convrot_gemm(p, 64, p, 64, p, p, None, p, 320, p, 320, 320, 4, 8, 64, p, 8, None) == lib.ERR_SHAPE
     assert L.convrot_lowrank_down(p, 64, p, 64, 4, 64, 300, p, 304, None) == lib.ERR_SHAPE
 
 

@@ -168,7 +168,8 @@ def test_lowrank_down_within_one_bf16_ulp(M, K, r):
 @pytest.mark.parametrize("M,K,N,r,group", [
     (40, 1024, 256, 16, 256), (333, 4096, 5120, 32, 256), (256, 4096, 5120, 32, 256), (256, 5120, 512, 64, 256),
     (17, 512, 300, 48, 16), (130, 2048, 1000, 0, 64),
-])  # (256 | 333, 4096 -> 5120, r = 32): config 5
+    (300, 1024, 512, 128, 256), (129, 2048, 768, 192, 256), (520, 512, 256, 256, 256), (77, 1024, 320, 80, 256),
+])  # (256 | 333, 4096 -> 5120, r = 32): config 5; r > 64 streams the rank through the epilogue in chunks of 64
 def test_fused_bias_and_low_rank_within_tolerance(M, K, N, r, group, gemm_mode):
     x = synthetic.activations(M, K, seed=13)
     w = synthetic.linear_weights(K, N, rank=r, bias=True, group=group)
@@ -531,3 +532,21 @@ def test_fused_swiglu_gate_first_and_shape_checks():
     q, s = I.rotate_quant(x, 256)
     with pytest.raises(ValueError):
         I.convrot_matmul(q, proj.qweight[:480], s, proj.wscale[:480], swiglu=True)  # 480 % 64 != 0
+
+
+def test_q_k_v_with_wide_ranks_fall_back_to_separate_down_projections():
+    """share_lowrank on three rank-128 layers (384 > 256 outputs for one down GEMM) still gives the separate results."""
+    def layer(seed):
+        w = synthetic.linear_weights(512, 256, rank=128, bias=True, group=256, seed_offset=seed)
+        m = I.Int8RotLinear(512, 256, 256, bias=True, rank=128)
+        synthetic.load_into(m, w)
+        return m.to(DEV)
+
+    to_q, to_k, to_v = layer(0), layer(1), layer(2)
+    x = synthetic.activations(200, 512, seed=81).to(DEV)
+    separate = [to_q(x), to_k(x), to_v(x)]
+    I.share_lowrank(to_q, to_k, to_v)
+    to_q.keep_input = to_k.keep_input = True
+    shared = [to_q(x), to_k(x), to_v(x)]
+    for a, b in zip(separate, shared, strict=True):
+        assert torch.equal(a, b)
