@@ -439,10 +439,14 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
   const bool chunked = p.x_chunk != p.K;
+  const bool adaln = p.mod_scale != nullptr;
+  if (adaln && (chunked || slots != 1)) return CONVROT_ERR_SHAPE;
   if (chunked && slots == 1 && threads > kRQ256ChunkedThreads) return launch_rq<256>(st, p, stream);
   const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
   void (*kernel)(const RotQuantParams) = nullptr;
-  if (slots == 1 && !chunked)
+  if (adaln)
+    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, false, true> : rotate_quant256_kernel<1, 0, false, true>;
+  else if (slots == 1 && !chunked)
     kernel = torch_rounding ? rotate_quant256_kernel<1, 1, false> : rotate_quant256_kernel<1, 0, false>;
   else if (slots == 1)
     kernel = torch_rounding ? rotate_quant256_kernel<1, 1, true> : rotate_quant256_kernel<1, 0, true>;
@@ -550,6 +554,50 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
   }
 }
 
+// The AdaLN-modulated rotate+quantise: the rotated row is h = modulate(LayerNorm(x)) (RotQuantParams), and h is
+// also stored to h_out when given.  The two-column kernel only (group 256, K <= 8192, plain rows).
+int rotate_quant_adaln(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding, const void* scale,
+                       const void* shift, const int32_t* index, int64_t ld_mod, float eps, int8_t* q, int64_t ldq,
+                       float* s, void* h_out, int64_t ld_h, cudaStream_t stream) {
+  if (group != 256) return CONVROT_ERR_GROUP;
+  if (M < 0 || K <= 0 || K % 256 || K > 8192 || ldx < K || ldq < K || ld_mod < K || M > INT32_MAX)
+    return CONVROT_ERR_SHAPE;
+  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
+  if (!(eps >= 0.0f)) return CONVROT_ERR_ARG;
+  if (h_out && ld_h < K) return CONVROT_ERR_SHAPE;
+  if (M == 0) return CONVROT_OK;
+  if (!x || !q || !s || !scale || !shift || !index) return CONVROT_ERR_ARG;
+  if (ldx % 8 || ldq % 16 || ld_mod % 8 || !aligned16(x) || !aligned16(q) || !aligned16(scale) || !aligned16(shift))
+    return CONVROT_ERR_ALIGN;
+  if (h_out && (ld_h % 8 || !aligned16(h_out))) return CONVROT_ERR_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  RotQuantParams p;
+  memset(&p, 0, sizeof(p));
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.xs[0] = p.x;
+  p.ldx = ldx;
+  p.x_chunk = static_cast<int>(K);
+  p.x_out = static_cast<__nv_bfloat16*>(h_out);
+  p.ld_out = ld_h;
+  p.mod_scale = static_cast<const __nv_bfloat16*>(scale);
+  p.mod_shift = static_cast<const __nv_bfloat16*>(shift);
+  p.mod_index = index;
+  p.ld_mod = ld_mod;
+  p.norm_eps = eps;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.q = q;
+  p.ldq = ldq;
+  p.s = s;
+  p.rounding = rounding;
+  p.stages = kRQMaxStages;
+  p.wait_limit_ns = g_wait_limit_ns;
+  p.error_word = st->error_word;
+  return launch_rq256(*st, p, stream);
+}
+
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 // Bytes convrot_linear needs for q (int8 [M, ldq]), s (fp32 [M]) and xa (bf16 [M, ldxa]), each 256-byte aligned.
@@ -603,6 +651,14 @@ int convrot_rotate_quant_packed(const void* x, int64_t chunk_cols, int64_t M, in
   for (int j = 0; j < n; ++j) chunks[j] = static_cast<const uint8_t*>(x) + j * M * chunk_cols * 2;
   return rotate_quant(x, chunk_cols, M, K, group, rounding, q_out, ldq, s_out, static_cast<cudaStream_t>(stream),
                       chunks, n);
+}
+
+int convrot_rotate_quant_adaln(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding,
+                               const void* mod_scale, const void* mod_shift, const int32_t* mod_index, int64_t ld_mod,
+                               float eps, int8_t* q_out, int64_t ldq, float* s_out, void* h_out, int64_t ld_h,
+                               void* stream) {
+  return rotate_quant_adaln(x, ldx, M, K, group, rounding, mod_scale, mod_shift, mod_index, ld_mod, eps, q_out, ldq,
+                            s_out, h_out, ld_h, static_cast<cudaStream_t>(stream));
 }
 
 int convrot_rotate_quant_gather(const void* const* x_chunks, int n_chunks, int64_t ldx, int64_t M, int64_t K,

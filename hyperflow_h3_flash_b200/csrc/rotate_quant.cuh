@@ -35,8 +35,16 @@ struct RotQuantParams {
   const __nv_bfloat16* xs[kMaxChunks];
   int64_t ldx;
   int x_chunk;
-  __nv_bfloat16* x_out;  // optional: each gathered bf16 row is also stored to x_out + m * ld_out (null: not)
+  __nv_bfloat16* x_out;  // optional: each gathered (or modulated) bf16 row is also stored to x_out + m * ld_out
   int64_t ld_out;
+  // AdaLN prologue (two-column kernel, plain rows): the row that is rotated is
+  //   h = bf16( bf16( bf16(LayerNorm(x)) * bf16(1 + scale[idx]) ) + shift[idx] ),  idx = mod_index[m]
+  // with scale / shift rows of ld_mod elements; LayerNorm has no affine part and eps = norm_eps.
+  const __nv_bfloat16* mod_scale;
+  const __nv_bfloat16* mod_shift;
+  const int32_t* mod_index;
+  int64_t ld_mod;
+  float norm_eps;
   int M, K;
   int8_t* q;
   int64_t ldq;
@@ -340,7 +348,27 @@ __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stage
   const size_t slots = static_cast<size_t>(K / 256) * kSlotBytes;
   const size_t tr = static_cast<size_t>(threads / 8) * 8 * kTrRow * 8;  // per team: 8 rows of the half transpose
   const size_t table = chunked ? static_cast<size_t>(K / 256) * sizeof(RQ256Piece) : 0;
-  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + table + 64;
+  const size_t stats = 64 * 8;  // AdaLN: per-warp (sum, sum of squares) in fp64
+  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + stats + table + 64;
+}
+
+// AdaLN on a pair of bf16 values (low half = even column): n = bf16((x - mean) * rstd) in fp32, then
+// bf16(bf16(n * bf16(1 + scale)) + shift), each step rounded to bf16 as the unfused bf16 tensor ops round it.
+__device__ __forceinline__ uint32_t adaln_pair(uint32_t w, uint32_t sc, uint32_t sh, float mean, float rstd) {
+  uint32_t out = 0;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int shift = 16 * half;
+    const float x = __uint_as_float(((w >> shift) & 0xffffu) << 16);
+    const float s = __uint_as_float(((sc >> shift) & 0xffffu) << 16);
+    const float b = __uint_as_float(((sh >> shift) & 0xffffu) << 16);
+    const float n = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fsub_rn(x, mean), rstd)));
+    const float one_s = __bfloat162float(__float2bfloat16_rn(__fadd_rn(1.0f, s)));
+    const float t = __bfloat162float(__float2bfloat16_rn(__fmul_rn(n, one_s)));
+    const __nv_bfloat16 h = __float2bfloat16_rn(__fadd_rn(t, b));
+    out |= static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&h)) << shift;
+  }
+  return out;
 }
 
 // CHUNKED selects the chunked-row input (the Ulysses layouts, in this GPU's memory or gathered from the others'):
@@ -348,7 +376,7 @@ __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stage
 // the plain walk costs, and x_out may receive each gathered row.  Plain rows (x_chunk == K) use the instantiation
 // without it.  The launch sizes residency from the compiled register count; at K = 5120 (160 threads) both forms
 // stay within 96 (plain 86 with no bound; chunked under its thread bound), so four CTAs fit an SM.
-template <int SLOTS, int ROUNDING, bool CHUNKED>
+template <int SLOTS, int ROUNDING, bool CHUNKED, bool ADALN = false>
 __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads : 512, CHUNKED && SLOTS == 1 ? 2 : 0)
     rotate_quant256_kernel(const RotQuantParams p) {
   extern __shared__ __align__(1024) uint8_t rq2_smem_raw[];
@@ -361,8 +389,9 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
   double* tr = reinterpret_cast<double*>(rq2_smem_raw + stages * stage_bytes);
   float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr / 8) * 8 * kTrRow);
   uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 32);
+  double* stats = reinterpret_cast<double*>(bars + kRQMaxStages);  // ADALN: (sum, sum of squares) per warp
   // CHUNKED: per group, the source offsets (elements from the row start) and byte counts of its one or two pieces
-  RQ256Piece* pieces = reinterpret_cast<RQ256Piece*>(bars + kRQMaxStages);
+  RQ256Piece* pieces = reinterpret_cast<RQ256Piece*>(stats + 64);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -437,6 +466,50 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
 
+    // AdaLN: the row's mean and 1/sqrt(var + eps), from fp64 sums (exact for bf16 rows of moderate range),
+    // each rounded once to fp32
+    float mean_f = 0.0f, rstd_f = 0.0f;
+    const uint32_t* scale_row = nullptr;
+    const uint32_t* shift_row = nullptr;
+    if constexpr (ADALN) {
+      const int64_t idx = __ldg(p.mod_index + m);
+      scale_row = reinterpret_cast<const uint32_t*>(p.mod_scale + idx * p.ld_mod);
+      shift_row = reinterpret_cast<const uint32_t*>(p.mod_shift + idx * p.ld_mod);
+      double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+      for (int sl = 0; sl < SLOTS; ++sl) {
+        const int g = (tid + sl * nthr) >> 3;
+        if (g >= ngroups) continue;
+        const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlotBytes) + tt;
+#pragma unroll
+        for (int a = 0; a < 16; ++a) {
+          const uint32_t w = col[a * 8];
+          const double x0 = __uint_as_float(w << 16), x1 = __uint_as_float(w & 0xffff0000u);
+          s1 += x0 + x1;
+          s2 = fma(x0, x0, fma(x1, x1, s2));
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, off);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, off);
+      }
+      if (lane == 0) {
+        stats[2 * warp] = s1;
+        stats[2 * warp + 1] = s2;
+      }
+      __syncthreads();
+      double t1 = 0.0, t2 = 0.0;
+      for (int w = 0; w < nwarps; ++w) {
+        t1 += stats[2 * w];
+        t2 += stats[2 * w + 1];
+      }
+      const double mean = t1 / K;
+      const double var = fmax(t2 / K - mean * mean, 0.0);
+      mean_f = __double2float_rn(mean);
+      rstd_f = __double2float_rn(1.0 / sqrt(var + static_cast<double>(p.norm_eps)));
+    }
+
     float y[SLOTS][32];
     float amax = 0.0f;
 #pragma unroll
@@ -452,7 +525,13 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlotBytes) + tt;
 #pragma unroll
       for (int a = 0; a < 16; ++a) {
-        const uint32_t w = col[a * 8];
+        uint32_t w = col[a * 8];
+        if constexpr (ADALN) {
+          // element (a, 2tt) of the group is column 256 g + 16 a + 2 tt of the row
+          w = adaln_pair(w, __ldg(scale_row + g * 128 + a * 8 + tt), __ldg(shift_row + g * 128 + a * 8 + tt), mean_f,
+                         rstd_f);
+          const_cast<uint32_t*>(col)[a * 8] = w;  // h replaces x in the row buffer (stored to x_out below)
+        }
         c0[a] = static_cast<double>(__uint_as_float(w << 16));
         c1[a] = static_cast<double>(__uint_as_float(w & 0xffff0000u));
       }
@@ -494,10 +573,19 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     if (lane == 0) warp_max[warp] = amax;
+    if constexpr (ADALN) fence_proxy_async_smem();  // h in the row buffer, for the bulk stores below
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) record_error_rq(p.error_word);
       aborted = true;
       break;
+    }
+    if constexpr (ADALN) {
+      if (tt == 0 && p.x_out) {  // each team stores its groups of h
+#pragma unroll 1
+        for (int g = tid >> 3; g < ngroups; g += nthr >> 3)
+          bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out + g * 256, xr + g * kSlotBytes, 512);
+        bulk_commit_group();
+      }
     }
     float rmax = 0.0f;
     for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
@@ -528,7 +616,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
     if (tid == 0) p.s[m] = scale;
-    if constexpr (CHUNKED) {
+    if constexpr (CHUNKED || ADALN) {
       if (tt == 0 && p.x_out) bulk_wait_group_read<0>();  // the row stores have read this buffer
     }
     __syncthreads();
@@ -537,7 +625,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       if (m_next < p.M) issue_row(st, m_next);
     }
   }
-  if constexpr (CHUNKED) {
+  if constexpr (CHUNKED || ADALN) {
     if (tt == 0 && p.x_out) bulk_wait_group_all();
   }
   if (aborted && tid == 0) {

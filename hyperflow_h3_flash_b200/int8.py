@@ -373,6 +373,49 @@ def rotate_quant_gather(x_ptrs: list[int], ldx: int, M: int, K: int, group: int,
     return q, s, x
 
 
+def rotate_quant_adaln(x: Tensor, group: int, scale: Tensor, shift: Tensor, index: Tensor, eps: float = 1e-6,
+                       rounding: int = _lib.ROUND_KERNEL) -> tuple[Tensor, Tensor, Tensor]:
+    """``rotate_quant`` of ``h = LN(x) * (1 + scale[index]) + shift[index]`` (bf16 steps, LayerNorm without affine
+    parameters), computed inside the kernel; returns ``(q, s, h)``.  ``scale`` / ``shift``: bf16 ``[T, K]``,
+    ``index``: ``[M]`` integers in ``[0, T)`` (the reference's ``adaln_indices``, transformer.py:345-348)."""
+    _require(x, "x", torch.bfloat16, 2)
+    M, K = x.shape
+    x = x.contiguous()
+    scale = scale.to(torch.bfloat16).contiguous()
+    shift = shift.to(torch.bfloat16).contiguous()
+    if scale.shape != shift.shape or scale.dim() != 2 or scale.shape[1] != K:
+        raise ValueError(f"scale / shift must be [T, {K}], got {tuple(scale.shape)} / {tuple(shift.shape)}")
+    index = index.to(device=x.device, dtype=torch.int32).contiguous()
+    if index.shape != (M,):
+        raise ValueError(f"index must be [{M}], got {tuple(index.shape)}")
+    q = torch.empty(M, K, dtype=torch.int8, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    h = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    rc = _lib.lib().convrot_rotate_quant_adaln(_ptr(x), K, M, K, group, rounding, _ptr(scale), _ptr(shift),
+                                               _ptr(index), K, float(eps), _ptr(q), K, _ptr(s), _ptr(h), K,
+                                               _stream(x))
+    _lib.check(rc, "convrot_rotate_quant_adaln")
+    return q, s, h
+
+
+def adaln_modulate_quantize(x: Tensor, scale: Tensor, shift: Tensor, index: Tensor, group: int,
+                            eps: float = 1e-6) -> Tensor:
+    """``h = norm(x) * (1 + scale[index]) + shift[index]`` for the q / k / v projections of a block, with their
+    shared quantisation computed in the same pass: returns h (bf16, for the low-rank down projection and anything
+    else that reads it) and leaves h's codes and scales in the ``keep_input`` cache, so ``to_q(h)`` (with
+    ``keep_input`` set, as the reference sets it for to_q / to_k) quantises nothing.  Call site: chunk_block,
+    transformer.py:345-353."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+    rounding = _lib.ROUND_KERNEL if x2.shape[0] >= _MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+    q, s, h = _kernels().rotate_quant_adaln(x2, group, scale, shift, index.reshape(-1), eps, rounding)
+    h = h.reshape(shape)
+    cache = Int8RotLinear._last_input
+    cache.clear()
+    cache.update(x=h, version=None if h.is_inference() else h._version, group=group, value=(q, s))
+    return h
+
+
 def rotate_quant_torch_rounding(x: Tensor, group: int) -> tuple[Tensor, Tensor]:
     """``rotate_quant`` with the reference torch path's rounding (bf16 rotation, division): int8.py:175-178."""
     return rotate_quant(x, group, _lib.ROUND_TORCH)
@@ -516,6 +559,7 @@ def _kernels() -> SimpleNamespace:
         rotate_quant_packed=rotate_quant_packed,
         lowrank_down_packed=lowrank_down_packed,
         rotate_quant_gather=rotate_quant_gather,
+        rotate_quant_adaln=rotate_quant_adaln,
     )
 
 

@@ -117,6 +117,21 @@ int convrot_lowrank_down_packed(const void* x, int64_t chunk_cols, const void* l
                                 int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
 
 /*
+ * AdaLN modulation fused into the rotate+quantise prologue (no counterpart in the reference; its call site is
+ * chunk_block, transformer.py:345-348, where the block computes h = norm1(x) * (1 + scale_msa[idx]) + shift_msa[idx]
+ * in bf16 tensor ops before to_q / to_k / to_v).  The rotated and quantised row is
+ *   h[m] = bf16( bf16( bf16(LN(x[m])) * bf16(1 + scale[idx[m]]) ) + shift[idx[m]] )
+ * with LN a LayerNorm without affine parameters (mean and 1/sqrt(var + eps) from fp64 sums, each rounded once to
+ * fp32; (x - mean) * rstd in fp32).  mod_scale / mod_shift are bf16 [T, K] (ld_mod), mod_index int32 [M] in [0, T).
+ * h_out (optional, bf16 [M, K], ld_h) receives h for the low-rank down projection.  group 256, K % 256 == 0,
+ * K <= 8192; other arguments as convrot_rotate_quant.
+ */
+int convrot_rotate_quant_adaln(const void* x, int64_t ldx, int64_t M, int64_t K, int group, int rounding,
+                               const void* mod_scale, const void* mod_shift, const int32_t* mod_index, int64_t ld_mod,
+                               float eps, int8_t* q_out, int64_t ldq, float* s_out, void* h_out, int64_t ld_h,
+                               void* stream);
+
+/*
  * The FFN's SwiGLU fused into the up projection's epilogue (no counterpart in the reference: diffusers' gated `net[0]`
  * runs `proj`, then `a, g = y.chunk(2, -1)`, then `a * silu(g)`; call site transformer.py:87-99).  The B operand is
  * the projection with its rows interleaved in 32-row blocks -- rows [64 j, 64 j + 32) are rows [32 j, 32 j + 32) of

@@ -233,6 +233,24 @@ def swiglu(y_bits: np.ndarray, gate_first: bool = False) -> np.ndarray:
     return f32_to_bf16((a * s).astype(np.float32))
 
 
+def adaln_modulate(x_bits: np.ndarray, scale_bits: np.ndarray, shift_bits: np.ndarray, index: np.ndarray,
+                   eps: float = 1e-6) -> np.ndarray:
+    """``h = norm1(x) * (1 + scale[idx]) + shift[idx]`` as the reference's chunk_block writes it
+    (transformer.py:346-348), each bf16 tensor op rounded to bf16, as bf16 bits.  ``norm1`` is diffusers' module
+    (absent here); this restates a LayerNorm without affine parameters: mean and variance of the row in float64,
+    ``mean`` and ``1/sqrt(var + eps)`` rounded once to float32, ``(x - mean) * rstd`` in float32."""
+    x32 = bf16_to_f32(x_bits)
+    x64 = x32.astype(np.float64)
+    mean = x64.mean(axis=1)
+    var = np.maximum((x64 * x64).mean(axis=1) - mean * mean, 0.0)
+    mean_f = mean.astype(np.float32)[:, None]
+    rstd_f = (1.0 / np.sqrt(var + np.float64(np.float32(eps)))).astype(np.float32)[:, None]
+    n = bf16_to_f32(f32_to_bf16(((x32 - mean_f).astype(np.float32) * rstd_f).astype(np.float32)))
+    one_s = bf16_to_f32(f32_to_bf16((np.float32(1) + bf16_to_f32(scale_bits)[index]).astype(np.float32)))
+    t = bf16_to_f32(f32_to_bf16((n * one_s).astype(np.float32)))
+    return f32_to_bf16((t + bf16_to_f32(shift_bits)[index]).astype(np.float32))
+
+
 def forward_cpu_port(x_bits: np.ndarray, qweight: np.ndarray, wscale: np.ndarray, group: int,
                      rotation: np.ndarray | None = None) -> np.ndarray:
     """numpy/BLAS port of the reference CPU path ``Int8RotLinear._forward_torch`` (int8.py:173-179).

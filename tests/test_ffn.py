@@ -47,3 +47,22 @@ def test_oracle_swiglu_matches_torch_cpu_within_one_ulp():
     got = O.swiglu(y.view(torch.int16).numpy().view(np.uint16))
     diff = np.abs(got.astype(np.int32) - ref.astype(np.int32))
     assert diff.max() <= 1 and (diff == 0).mean() >= 0.999
+
+
+def test_oracle_adaln_matches_torch_layer_norm_composition_within_one_ulp():
+    """The oracle's AdaLN restatement against the bf16 torch ops of chunk_block (transformer.py:346-348) with a
+    non-affine LayerNorm on CPU (torch's own statistics: differences of one bf16 ulp where a value sits next to a
+    rounding boundary)."""
+    g = torch.Generator().manual_seed(1)
+    M, K, T = 64, 1024, 3
+    x = (torch.randn(M, K, generator=g) * 2).to(torch.bfloat16)
+    x[:, ::97] *= 30
+    scale = (torch.randn(T, K, generator=g) * 0.1).to(torch.bfloat16)
+    shift = (torch.randn(T, K, generator=g) * 0.1).to(torch.bfloat16)
+    idx = torch.randint(0, T, (M,), generator=g)
+    n = F.layer_norm(x, (K,), eps=1e-6)
+    ref = n * (1.0 + scale.index_select(0, idx)) + shift.index_select(0, idx)
+    u16 = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    got = O.adaln_modulate(u16(x), u16(scale), u16(shift), idx.numpy())
+    diff = np.abs(got.astype(np.int32) - u16(ref).astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() >= 0.995

@@ -14,6 +14,7 @@ import os
 import numpy as np
 import pytest
 import torch
+import torch.nn.functional as F
 
 from hyperflow_h3_flash_b200 import _lib
 from hyperflow_h3_flash_b200 import int8 as I
@@ -549,4 +550,62 @@ def test_q_k_v_with_wide_ranks_fall_back_to_separate_down_projections():
     to_q.keep_input = to_k.keep_input = True
     shared = [to_q(x), to_k(x), to_v(x)]
     for a, b in zip(separate, shared, strict=True):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M,K,T", [(333, 5120, 4), (4096, 2048, 1), (8, 1024, 2), (17, 256, 3)])
+def test_adaln_prologue_is_the_oracle_and_quantises_its_own_h_bitwise(M, K, T):
+    """The AdaLN rotate kernel's h equals the oracle's restatement (fp64 statistics; at most one bf16 ulp where the
+    summation order moves a statistic's last bit), and its codes and scales are bitwise those of h."""
+    g = torch.Generator().manual_seed(M + K)
+    x = synthetic.activations(M, K, seed=91)
+    scale = (torch.randn(T, K, generator=g) * 0.1).to(torch.bfloat16)
+    shift = (torch.randn(T, K, generator=g) * 0.1).to(torch.bfloat16)
+    idx = torch.randint(0, T, (M,), generator=g)
+    rounding = _lib.ROUND_KERNEL if M >= I._MIN_KERNEL_ROWS else _lib.ROUND_TORCH
+    q, s, h = I.rotate_quant_adaln(x.to(DEV), 256, scale.to(DEV), shift.to(DEV), idx.to(DEV), 1e-6, rounding)
+    ref = O.adaln_modulate(bits(x), bits(scale), bits(shift), idx.numpy())
+    diff = np.abs(bits(h).astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() >= 0.9999
+    q_ref, s_ref = (O.rotate_quant if rounding == _lib.ROUND_KERNEL else O.rotate_quant_cpu)(bits(h), 256)
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+    # and against the bf16 torch ops of chunk_block on the GPU (torch's own LayerNorm statistics)
+    xd, sd, hd = x.to(DEV), scale.to(DEV), shift.to(DEV)
+    th = F.layer_norm(xd, (K,), eps=1e-6) * (1.0 + sd.index_select(0, idx.to(DEV))) + hd.index_select(0, idx.to(DEV))
+    d2 = np.abs(bits(h).astype(np.int32) - bits(th).astype(np.int32))
+    assert d2.max() <= 1 and (d2 == 0).mean() >= 0.995
+
+
+def test_adaln_modulate_quantize_feeds_the_q_k_v_projections():
+    """adaln_modulate_quantize leaves h's codes in the keep_input cache: q / k / v (with shared low-rank) give
+    exactly what the same layers give on h computed without the cache, and no rotate kernel runs for them."""
+    K, N, r, M = 1024, 512, 32, 300
+    layers = []
+    for i in range(3):
+        w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256, seed_offset=30 + i)
+        m = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+        synthetic.load_into(m, w)
+        layers.append(m.to(DEV))
+    to_q, to_k, to_v = layers
+    g = torch.Generator().manual_seed(5)
+    x = synthetic.activations(M, K, seed=92).to(DEV)
+    scale = (torch.randn(2, K, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    shift = (torch.randn(2, K, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    idx = (torch.arange(M) % 2).to(DEV)
+    h = I.adaln_modulate_quantize(x, scale, shift, idx, 256)
+    h_copy = h.clone()
+    separate = [to_q(h_copy), to_k(h_copy), to_v(h_copy)]
+    I.share_lowrank(to_q, to_k, to_v)
+    to_q.keep_input = to_k.keep_input = True
+    h = I.adaln_modulate_quantize(x, scale, shift, idx, 256)
+    kernels = I._kernels()
+    calls = []
+    rq = kernels.rotate_quant
+    kernels.rotate_quant = lambda *a: calls.append(1) or rq(*a)
+    try:
+        fused = [to_q(h), to_k(h), to_v(h)]
+    finally:
+        kernels.rotate_quant = rq
+    assert calls == []
+    for a, b in zip(separate, fused, strict=True):
         assert torch.equal(a, b)
