@@ -547,6 +547,27 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
                              "ms_unfused": ms_unfused, "ms_fused_swiglu": ms_fused}
     out["block_set_cfg3_swiglu"] = {"config": "config 3 with FFN-down reading the fused SwiGLU of FFN-up",
                                     "ms": ms_block, "tops": ops / (ms_block * 1e-3) / 1e12}
+
+    # the block's AdaLN prologue before q/k/v (chunk_block): h = LN(x) * (1 + scale[idx]) + shift[idx], quantised
+    import torch.nn.functional as F
+
+    frames = 8
+    gen = torch.Generator().manual_seed(9)
+    mod_scale = (torch.randn(frames, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
+    mod_shift = (torch.randn(frames, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
+    mod_idx = (torch.arange(Mb, device=dev) * frames // Mb).to(torch.int32)
+
+    def adaln_unfused():
+        hh = F.layer_norm(xb, (K_DIM,), eps=1e-6)
+        hh = hh * (1.0 + mod_scale.index_select(0, mod_idx)) + mod_shift.index_select(0, mod_idx)
+        return I.rotate_quant(hh, GROUP), hh
+
+    def adaln_fused():
+        return I.rotate_quant_adaln(xb, GROUP, mod_scale, mod_shift, mod_idx)
+
+    out["adaln_prologue_cfg3"] = {"config": "M=32760, K=5120, 8 modulation rows: LayerNorm + modulate + rotate+quantise",
+                                  "ms_unfused": timed(adaln_unfused, args.steps),
+                                  "ms_fused": timed(adaln_fused, args.steps)}
     return out
 
 

@@ -571,9 +571,13 @@ def test_adaln_prologue_is_the_oracle_and_quantises_its_own_h_bitwise(M, K, T):
     assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
     # and against the bf16 torch ops of chunk_block on the GPU (torch's own LayerNorm statistics)
     xd, sd, hd = x.to(DEV), scale.to(DEV), shift.to(DEV)
-    th = F.layer_norm(xd, (K,), eps=1e-6) * (1.0 + sd.index_select(0, idx.to(DEV))) + hd.index_select(0, idx.to(DEV))
-    d2 = np.abs(bits(h).astype(np.int32) - bits(th).astype(np.int32))
-    assert d2.max() <= 1 and (d2 == 0).mean() >= 0.995
+    tt = F.layer_norm(xd, (K,), eps=1e-6) * (1.0 + sd.index_select(0, idx.to(DEV)))
+    th = tt + hd.index_select(0, idx.to(DEV))
+    assert (h == th).float().mean().item() >= 0.995
+    # torch's fp32 statistics (Welford mean, rsqrt) can move n by an ulp, which moves t = n * (1 + scale) by up to
+    # two bf16 ulps, and t + shift can cancel: bound the difference by the final add's operands, not its result
+    bound = (tt.float().abs() + hd.index_select(0, idx.to(DEV)).float().abs()) * 2.0**-5
+    assert ((h.float() - th.float()).abs() <= bound).all()
 
 
 def test_adaln_modulate_quantize_feeds_the_q_k_v_projections():
