@@ -312,7 +312,20 @@ def run_ours(args) -> None:
 
     exchange = None
     if world > 1 and args.transport == "peer":
-        exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev)
+        # every rank must agree on the transport: a rank whose mapping fails tells the others through an all-reduce
+        try:
+            exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev)
+            failed = 0
+        except Exception as e:  # noqa: BLE001 - reported, and the NCCL transport is used instead
+            print(f"peer-memory exchange unavailable on rank {rank}: {e}; using NCCL all-to-all", file=sys.stderr)
+            failed = 1
+        flag = torch.tensor([failed], device=dev)
+        dist.all_reduce(flag)
+        if flag.item():
+            if exchange is not None:
+                exchange.close()
+            exchange = None
+            args.transport = "nccl"
 
     def step(inp):
         return ulysses.attention_block_linears(inp, to_q, to_k, to_v, to_out, HEADS, exchange=exchange)

@@ -109,27 +109,34 @@ class PeerExchange:
         self.buf = torch.zeros(self._FLAG_BYTES + len(self._NAMES) * self._tensor_bytes, dtype=torch.uint8,
                                device=self.device)
         L = _lib.lib()
+        # Every rank takes the same collective steps whether or not its own part fails, so a failure on one rank
+        # raises on all of them instead of leaving the others waiting.
         handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
         offset = ctypes.c_int64(0)
-        _lib.check(L.convrot_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(offset)),
-                   "convrot_ipc_handle")
+        rc = L.convrot_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(offset))
         everyone: list = [None] * self.P
-        dist.all_gather_object(everyone, (handle.raw, offset.value), group=group)
+        dist.all_gather_object(everyone, (handle.raw, offset.value) if rc == _lib.OK else None, group=group)
+        if any(e is None for e in everyone):
+            raise RuntimeError("a rank could not export its exchange buffer (CUDA IPC)")
         self._opened: list[int] = []
         self.base: list[int] = []
-        try:
-            for j, (h, off) in enumerate(everyone):
-                if j == self.rank:
-                    self.base.append(self.buf.data_ptr())
-                    continue
-                mapped = ctypes.c_void_p(0)
-                _lib.check(L.convrot_ipc_open(ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES),
-                                              ctypes.byref(mapped)), "convrot_ipc_open")
-                self._opened.append(mapped.value)
-                self.base.append(mapped.value + off)
-        except Exception:
+        error = None
+        for j, (h, off) in enumerate(everyone):
+            if j == self.rank:
+                self.base.append(self.buf.data_ptr())
+                continue
+            mapped = ctypes.c_void_p(0)
+            rc = L.convrot_ipc_open(ctypes.create_string_buffer(h, _lib.IPC_HANDLE_BYTES), ctypes.byref(mapped))
+            if rc != _lib.OK:
+                error = f"convrot_ipc_open of rank {j}: {_lib.status_string(rc)}"
+                break
+            self._opened.append(mapped.value)
+            self.base.append(mapped.value + off)
+        failed = torch.tensor([0 if error is None else 1], device=self.device)
+        dist.all_reduce(failed, group=group)
+        if failed.item():
             self._unmap()
-            raise
+            raise RuntimeError(error or "another rank could not map the exchange buffers")
         self.epoch = 0
         self.kernel_launches = 0
         torch.cuda.synchronize(self.device)

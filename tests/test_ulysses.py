@@ -98,3 +98,27 @@ def test_shapes_are_checked():
     t = torch.zeros(6, HEADS * D)
     assert ulysses.seq_to_head(t, HEADS).shape == (6, HEADS, D)  # single process: no exchange
     assert ulysses.head_to_seq(ulysses.seq_to_head(t, HEADS)).shape == (6, HEADS * D)
+
+
+def _worker_exchange_setup_fails(rank, world, store_path, out_path):
+    _init(rank, world, store_path)
+    try:
+        # host memory cannot be exported through CUDA IPC: every rank must get the error, none may hang
+        ulysses.PeerExchange(16, 8 * 128, 8, device=torch.device("cpu"))
+        result = "constructed"
+    except RuntimeError as e:
+        result = str(e)
+    finally:
+        dist.destroy_process_group()
+    torch.save(result, f"{out_path}.{rank}")
+
+
+def test_peer_exchange_setup_failure_reaches_every_rank(tmp_path):
+    world = 2
+    ctx = mp.start_processes(_worker_exchange_setup_fails, args=(world, str(tmp_path / "store"), str(tmp_path / "out")),
+                             nprocs=world, join=False, start_method="spawn")
+    for p in ctx.processes:
+        p.join(timeout=120)
+    assert all(not p.is_alive() for p in ctx.processes)
+    for rank in range(world):
+        assert "could not export" in torch.load(f"{tmp_path / 'out'}.{rank}")
