@@ -241,14 +241,29 @@ using Cfg2 = Gemm2Cfg<5, 0, 0>;
 using Cfg2LR32 = Gemm2Cfg<5, 64, 1>;
 using Cfg2LR64 = Gemm2Cfg<5, 128, 1>;
 
+struct ResidualArgs {
+  const void* res;
+  int64_t ld_res;
+  const void* gate;
+  int64_t ld_gate;
+  const int32_t* gate_index;
+};
+
 // n_chunks > 1 writes the bf16 output in column chunks of N / n_chunks: chunk j as [M, ldo] rows at chunks[j] (the
 // Ulysses send layout, or the receive buffers of the other GPUs); `out` is then ignored.
 int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
             int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream,
-            void* const* chunks = nullptr, int n_chunks = 1, bool swiglu = false) {
+            void* const* chunks = nullptr, int n_chunks = 1, bool swiglu = false,
+            const ResidualArgs* residual = nullptr) {
   if (n_chunks < 1 || n_chunks > kMaxChunks || (n_chunks > 1 && !chunks)) return CONVROT_ERR_ARG;
   if (swiglu && (raw || n_chunks > 1)) return CONVROT_ERR_ARG;
+  if (residual) {
+    if (raw || swiglu || n_chunks > 1 || !residual->res) return CONVROT_ERR_ARG;
+    if (residual->ld_res < N || (residual->gate && residual->ld_gate < N)) return CONVROT_ERR_SHAPE;
+    if (residual->ld_res % 8 || !aligned16(residual->res)) return CONVROT_ERR_ALIGN;
+    if (residual->gate && (residual->ld_gate % 8 || !aligned16(residual->gate))) return CONVROT_ERR_ALIGN;
+  }
   if (swiglu && N % 64) return CONVROT_ERR_SHAPE;
   int64_t out_chunk = swiglu ? N / 2 : N;
   if (n_chunks > 1) {
@@ -309,6 +324,13 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.ldo = ldo;
   p.out_chunk = static_cast<int>(out_chunk);
   p.swiglu = swiglu ? 1 : 0;
+  if (residual) {
+    p.res = static_cast<const __nv_bfloat16*>(residual->res);
+    p.ld_res = residual->ld_res;
+    p.gate = static_cast<const __nv_bfloat16*>(residual->gate);
+    p.ld_gate = residual->ld_gate;
+    p.gate_index = residual->gate_index;
+  }
   p.a_chunk = static_cast<int>(K);
   p.r = has_lr ? static_cast<int>(r) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
@@ -686,6 +708,16 @@ int convrot_gemm_packed(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
   for (int j = 0; j < n; ++j) chunks[j] = static_cast<uint8_t*>(y) + j * M * chunk_cols * 2;
   return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, chunk_cols, false,
                  static_cast<cudaStream_t>(stream), chunks, n);
+}
+
+int convrot_gemm_residual(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
+                          const float* ws, const void* bias, const void* xa, int64_t ldxa, const void* lr_up,
+                          int64_t ld_up, int64_t r, int64_t M, int64_t N, int64_t K, const void* res, int64_t ld_res,
+                          const void* gate, int64_t ld_gate, const int32_t* gate_index, void* y, int64_t ldy,
+                          void* stream) {
+  const ResidualArgs args{res, ld_res, gate, ld_gate, gate_index};
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, y, ldy, false,
+                 static_cast<cudaStream_t>(stream), nullptr, 1, false, &args);
 }
 
 int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,

@@ -47,6 +47,13 @@ struct GemmParams {
   int out_chunk;        // columns per chunk (N for plain rows, out_chunks[0] == out)
   int swiglu;           // 1: the B rows are a SwiGLU projection interleaved in 32-row blocks (a0 g0 a1 g1 ...);
                         //    the bf16 output is h = a * silu(g), [M, N / 2]
+  // Gated residual (res != null): out = bf16(res + bf16(gate[idx] * bf16(y))), idx = gate_index[row] (0 without an
+  // index), and out = bf16(res + bf16(y)) without a gate.
+  const __nv_bfloat16* res;
+  int64_t ld_res;
+  const __nv_bfloat16* gate;
+  int64_t ld_gate;
+  const int32_t* gate_index;
   int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
   uint64_t wait_limit_ns;
@@ -172,6 +179,54 @@ __device__ __forceinline__ void store_bf16_chunk(__nv_bfloat16* dst, const float
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (n + j < N) dst[j] = __float2bfloat16_rn(t[j]);
+  }
+}
+
+// The gated residual on 32 output columns [n, n + 32) of one row (row < M): t holds the linear's fp32 values and
+// becomes bf16(res + bf16(gate * bf16(t))) -- the bf16 tensor ops `res + gate * linear(x)` -- columns at or beyond
+// N give 0 (they are not stored).
+__device__ __forceinline__ void gated_residual(float (&t)[32], const GemmParams& p, int row, int n) {
+  const __nv_bfloat16* rrow = p.res + static_cast<int64_t>(row) * p.ld_res + n;
+  const __nv_bfloat16* grow = nullptr;
+  if (p.gate) grow = p.gate + static_cast<int64_t>(p.gate_index ? __ldg(p.gate_index + row) : 0) * p.ld_gate + n;
+  uint32_t r[16], g[16];
+  if (n + 32 <= p.N) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(rrow) + j);
+      r[4 * j] = u.x;
+      r[4 * j + 1] = u.y;
+      r[4 * j + 2] = u.z;
+      r[4 * j + 3] = u.w;
+      if (grow) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(grow) + j);
+        g[4 * j] = v.x;
+        g[4 * j + 1] = v.y;
+        g[4 * j + 2] = v.z;
+        g[4 * j + 3] = v.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const bool in0 = n + 2 * j < p.N, in1 = n + 2 * j + 1 < p.N;
+      const uint32_t r0 = in0 ? __bfloat16_as_ushort(rrow[2 * j]) : 0u;
+      const uint32_t r1 = in1 ? __bfloat16_as_ushort(rrow[2 * j + 1]) : 0u;
+      r[j] = r0 | (r1 << 16);
+      if (grow) {
+        const uint32_t g0 = in0 ? __bfloat16_as_ushort(grow[2 * j]) : 0u;
+        const uint32_t g1 = in1 ? __bfloat16_as_ushort(grow[2 * j + 1]) : 0u;
+        g[j] = g0 | (g1 << 16);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int sh = (j & 1) ? 0 : 16;
+    const float rj = __uint_as_float((r[j >> 1] << sh) & 0xffff0000u);
+    float v = __bfloat162float(__float2bfloat16_rn(t[j]));
+    if (grow) v = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__uint_as_float((g[j >> 1] << sh) & 0xffff0000u), v)));
+    t[j] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(rj, v)));
   }
 }
 
@@ -509,7 +564,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
           } else if (!p.swiglu) {
-            if (row_ok) store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
+            if (row_ok) {
+              if (p.res) gated_residual(t, p, row, n);
+              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
+            }
           } else if (swiglu_block(t, c, ya) && row_ok) {
             store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n - 32) >> 1), t, (n - 32) >> 1, n_out);
           }
@@ -534,9 +592,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            if (!p.swiglu)
+            if (!p.swiglu) {
+              if (p.res) gated_residual(t, p, row, n0 + c);
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
-            else if (swiglu_block(t, c, ya))
+            } else if (swiglu_block(t, c, ya))
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n0 + c - 32) >> 1), t, (n0 + c - 32) >> 1, n_out);
           }
         }

@@ -487,6 +487,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
             tmem_st_32x32b_x32(taddr + c, w);
           } else if (!p.swiglu) {
+            if (p.res && row_ok) gated_residual(t, p, row, n);
             stage_and_store(t, m0 + quad * 32, n);  // rows beyond M are clipped by the TMA store
           } else if (swiglu_block(t, c, ya)) {
             stage_and_store(t, m0 + quad * 32, (n - 32) >> 1);
@@ -510,9 +511,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            if (!p.swiglu)
+            if (!p.swiglu) {
+              if (p.res && row_ok) gated_residual(t, p, row, n0 + c);
               stage_and_store(t, m0 + quad * 32, n0 + c);
-            else if (swiglu_block(t, c, ya))
+            } else if (swiglu_block(t, c, ya))
               stage_and_store(t, m0 + quad * 32, (n0 + c - 32) >> 1);
           }
         }

@@ -163,9 +163,22 @@ class Int8RotLinear(nn.Module):
             start += layer.rank
         return fused[:, start:start + self.rank]
 
-    def forward(self, x: Tensor, *, out_chunks: int | None = None) -> Tensor:
+    def forward(self, x: Tensor, *, out_chunks: int | None = None, residual: Tensor | None = None,
+                gate: Tensor | None = None, gate_index: Tensor | None = None) -> Tensor:
         """``out_chunks = P`` (CUDA only) returns the output packed for the Ulysses all-to-all: ``[P, M, N / P]``,
-        column block j of every row in ``[j]`` (see ``forward_packed`` for the matching input)."""
+        column block j of every row in ``[j]`` (see ``forward_packed`` for the matching input).
+
+        ``residual`` returns ``residual + gate[gate_index] * self(x)`` in bf16 steps, the block's gated residual
+        (transformer.py:375, 378), fused into the GEMM epilogue on CUDA."""
+        if residual is not None and not x.is_cuda:  # the same bf16 tensor ops, unfused
+            y = self.forward(x)
+            if gate is not None:
+                rows = gate.reshape(-1, self.out_features)
+                if gate_index is not None:
+                    y = rows.index_select(0, gate_index.reshape(-1)).reshape(y.shape) * y
+                else:
+                    y = rows[0] * y
+            return residual + y
         shape = x.shape
         x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
         if x2.is_cuda:
@@ -178,7 +191,8 @@ class Int8RotLinear(nn.Module):
                 xq, sx = kernels.rotate_quant_torch_rounding(x2, self.group)
             xa = self._lowrank_input(x2, kernels) if self.rank else None
             y = kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
-                                       up=self.up.weight if self.rank else None, out_chunks=out_chunks)
+                                       up=self.up.weight if self.rank else None, out_chunks=out_chunks,
+                                       residual=residual, gate=gate, gate_index=gate_index)
             if out_chunks:
                 return y
         else:
@@ -443,13 +457,16 @@ def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
 def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor | None = None,
                    xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None,
                    out_ptrs: list[int] | None = None, out_ld: int | None = None,
-                   swiglu: bool = False) -> Tensor | None:
+                   swiglu: bool = False, residual: Tensor | None = None, gate: Tensor | None = None,
+                   gate_index: Tensor | None = None) -> Tensor | None:
     """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
 
     ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout).  ``out_ptrs`` (device
     addresses, possibly in other GPUs' memory) writes column chunk j as ``[M, out_ld]`` rows at ``out_ptrs[j]`` and
     returns None: the Ulysses exchange done by the GEMM's stores.  ``swiglu`` treats b (and sb, bias, up) as a gated
-    projection interleaved in 32-row blocks (``ffn.interleave_rows``) and returns ``h = a * silu(g)``, ``[M, N / 2]``."""
+    projection interleaved in 32-row blocks (``ffn.interleave_rows``) and returns ``h = a * silu(g)``, ``[M, N / 2]``.
+    ``residual`` (bf16 ``[M, N]``) returns ``residual + gate[gate_index] * y`` in bf16 steps (``gate`` bf16
+    ``[T, N]`` or ``[N]``, optional; ``gate_index`` ``[M]``, optional: row 0 for every token)."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -479,6 +496,25 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         lr = -(-r // 8) * 8
         xa = _pad_cols(xa.to(torch.bfloat16), lr)
         up = _pad_cols(up.to(torch.bfloat16).contiguous(), lr)
+    if residual is not None:
+        if swiglu or out_ptrs is not None or out_chunks:
+            raise ValueError("a residual goes with one plain [M, N] output")
+        res = residual.reshape(M, N).to(torch.bfloat16)
+        res = res if (res.stride(1) == 1 and res.stride(0) % 8 == 0 and res.data_ptr() % 16 == 0) else res.contiguous()
+        g = None if gate is None else gate.reshape(-1, N).to(torch.bfloat16).contiguous()
+        gi = None
+        if gate_index is not None:
+            gi = gate_index.reshape(-1).to(device=a.device, dtype=torch.int32).contiguous()
+            if gi.numel() != M or g is None:
+                raise ValueError("gate_index needs a gate and one index per row")
+        ldy = -(-N // 8) * 8
+        y = torch.empty(M, ldy, dtype=torch.bfloat16, device=a.device)
+        rc = _lib.lib().convrot_gemm_residual(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                              _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                              up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(res),
+                                              res.stride(0), _ptr(g), N, _ptr(gi), _ptr(y), ldy, _stream(a))
+        _lib.check(rc, "convrot_gemm_residual")
+        return y if ldy == N else y[:, :N]
     if swiglu:
         if out_ptrs is not None or out_chunks:
             raise ValueError("swiglu writes one plain [M, N / 2] output")

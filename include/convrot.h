@@ -132,6 +132,20 @@ int convrot_rotate_quant_adaln(const void* x, int64_t ldx, int64_t M, int64_t K,
                                void* stream);
 
 /*
+ * A gated residual fused into the GEMM epilogue (no counterpart in the reference; its call sites are chunk_block's
+ * `h = x + gate_msa[idx] * to_out(o)` and `out = h + gate_mlp[idx] * ff(n)`, transformer.py:374-378, bf16 tensor ops):
+ *   y[m, n] = bf16( res[m, n] + bf16( gate[idx[m], n] * bf16(linear[m, n]) ) )
+ * with linear[m, n] the convrot_gemm value (bias and low-rank included).  res bf16 [M, N] (ld_res); gate bf16 [T, N]
+ * (ld_gate) or NULL (y = bf16(res + bf16(linear))); gate_index int32 [M] or NULL (row 0 of gate for every token).
+ * y may be res (same leading dimension): each element is read before it is written.
+ */
+int convrot_gemm_residual(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx,
+                          const float* ws, const void* bias, const void* xa, int64_t ldxa, const void* lr_up,
+                          int64_t ld_up, int64_t r, int64_t M, int64_t N, int64_t K, const void* res, int64_t ld_res,
+                          const void* gate, int64_t ld_gate, const int32_t* gate_index, void* y, int64_t ldy,
+                          void* stream);
+
+/*
  * The FFN's SwiGLU fused into the up projection's epilogue (no counterpart in the reference: diffusers' gated `net[0]`
  * runs `proj`, then `a, g = y.chunk(2, -1)`, then `a * silu(g)`; call site transformer.py:87-99).  The B operand is
  * the projection with its rows interleaved in 32-row blocks -- rows [64 j, 64 j + 32) are rows [32 j, 32 j + 32) of

@@ -613,3 +613,44 @@ def test_adaln_modulate_quantize_feeds_the_q_k_v_projections():
     assert calls == []
     for a, b in zip(separate, fused, strict=True):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("M,K,N,r,T", [(333, 5120, 5120, 32, 4), (4096, 1024, 2048, 0, 1), (17, 512, 300, 64, 2),
+                                        (8, 1024, 256, 16, 3)])
+def test_gated_residual_epilogue_is_bitwise_the_bf16_composition(M, K, N, r, T, gemm_mode):
+    """Int8RotLinear(x, residual=, gate=, gate_index=) equals `residual + gate[idx] * layer(x)` in bf16 torch ops."""
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256, seed_offset=40)
+    layer = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+    synthetic.load_into(layer, w)
+    layer = layer.to(DEV)
+    g = torch.Generator().manual_seed(M)
+    x = synthetic.activations(M, K, seed=93).to(DEV)
+    res = synthetic.activations(M, N, seed=94).to(DEV)
+    gate = (torch.randn(T, N, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    idx = torch.randint(0, T, (M,), generator=g).to(DEV)
+    y = layer(x)
+    assert torch.equal(layer(x, residual=res, gate=gate, gate_index=idx), res + gate.index_select(0, idx) * y)
+    assert torch.equal(layer(x, residual=res, gate=gate[0]), res + gate[0] * y)
+    assert torch.equal(layer(x, residual=res), res + y)
+
+
+def test_gated_residual_in_place_through_the_c_abi():
+    """convrot_gemm_residual with y == res overwrites the residual stream with the result."""
+    import ctypes
+
+    M, K, N = 300, 1024, 512
+    w = synthetic.linear_weights(K, N, rank=0, bias=False, group=256, seed_offset=41).to(DEV)
+    x = synthetic.activations(M, K, seed=95).to(DEV)
+    res = synthetic.activations(M, N, seed=96).to(DEV)
+    gate = (torch.randn(2, N) * 0.3).to(torch.bfloat16).to(DEV)
+    idx = (torch.arange(M) % 2).to(torch.int32).to(DEV)
+    q, s = I.rotate_quant(x, 256)
+    expected = res + gate.index_select(0, idx.long()) * I.convrot_matmul(q, w.qweight, s, w.wscale)
+    P = ctypes.c_void_p
+    buf = res.clone()
+    rc = _lib.lib().convrot_gemm_residual(P(q.data_ptr()), K, P(w.qweight.data_ptr()), K, P(s.data_ptr()),
+                                          P(w.wscale.data_ptr()), None, None, 0, None, 0, 0, M, N, K,
+                                          P(buf.data_ptr()), N, P(gate.data_ptr()), N, P(idx.data_ptr()),
+                                          P(buf.data_ptr()), N, P(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "convrot_gemm_residual")
+    assert torch.equal(buf, expected)

@@ -138,3 +138,22 @@ def test_oracle_semantics_differ_from_cpu_path_only_by_the_rotation_rounding():
     qc, sc = O.rotate_quant_cpu(xb, 256)
     assert np.abs(qk.astype(int) - qc).max() <= 1
     np.testing.assert_allclose(sk, sc, rtol=1e-2)
+
+
+def test_gated_residual_on_cpu_is_the_bf16_composition():
+    import torch
+
+    from hyperflow_h3_flash_b200 import int8 as I
+    from hyperflow_h3_flash_b200 import synthetic
+
+    w = synthetic.linear_weights(512, 256, rank=16, bias=True, group=256)
+    layer = I.Int8RotLinear(512, 256, 256, bias=True, rank=16)
+    synthetic.load_into(layer, w)
+    x = synthetic.activations(20, 512, seed=3)
+    res = synthetic.activations(20, 256, seed=4)
+    gate = (torch.randn(3, 256) * 0.1).to(torch.bfloat16)
+    idx = torch.arange(20) % 3
+    y = layer(x)
+    assert torch.equal(layer(x, residual=res, gate=gate, gate_index=idx), res + gate.index_select(0, idx) * y)
+    assert torch.equal(layer(x, residual=res, gate=gate[1]), res + gate[1] * y)
+    assert torch.equal(layer(x, residual=res), res + y)
