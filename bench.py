@@ -581,6 +581,36 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     out["adaln_prologue_cfg3"] = {"config": "M=32760, K=5120, 8 modulation rows: LayerNorm + modulate + rotate+quantise",
                                   "ms_unfused": timed(adaln_unfused, args.steps),
                                   "ms_fused": timed(adaln_fused, args.steps)}
+
+    # the whole block as chunk_block runs it (transformer.py:339-380), attention replaced by identity (o = v):
+    # AdaLN -> QKV -> out + gated residual -> AdaLN -> FFN-up -> SwiGLU -> FFN-down + gated residual
+    mods = [(torch.randn(frames, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev) for _ in range(6)]
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = mods
+    idx_l = mod_idx.long()
+
+    def block_unfused():
+        hh = F.layer_norm(xb, (K_DIM,), eps=1e-6)
+        hh = hh * (1.0 + scale_msa.index_select(0, idx_l)) + shift_msa.index_select(0, idx_l)
+        o = layers["qkv"](hh)[:, 2 * K_DIM:]
+        h2 = xb + gate_msa.index_select(0, idx_l) * layers["out"](o)
+        n = F.layer_norm(h2, (K_DIM,), eps=1e-6)
+        n = n * (1.0 + scale_mlp.index_select(0, idx_l)) + shift_mlp.index_select(0, idx_l)
+        f = layers["ffn_down"](ffn.swiglu_reference(layers["ffn_up"](n)))
+        return h2 + gate_mlp.index_select(0, idx_l) * f
+
+    def block_fused():
+        hh = I.adaln_modulate_quantize(xb, scale_msa, shift_msa, mod_idx, GROUP)
+        o = layers["qkv"](hh)[:, 2 * K_DIM:]
+        h2 = layers["out"](o, residual=xb, gate=gate_msa, gate_index=mod_idx)
+        n = I.adaln_modulate_quantize(h2, scale_mlp, shift_mlp, mod_idx, GROUP)
+        return layers["ffn_down"](swiglu_up(n), residual=h2, gate=gate_mlp, gate_index=mod_idx)
+
+    ms_bu = timed(block_unfused, max(3, args.steps // 2))
+    ms_bf = timed(block_fused, max(3, args.steps // 2))
+    out["dit_block_cfg3"] = {"config": "config 3 block dataflow (chunk_block with identity attention): AdaLN, QKV, "
+                                       "out + gated residual, AdaLN, FFN-up, SwiGLU, FFN-down + gated residual",
+                             "ms_unfused": ms_bu, "ms_fused": ms_bf, "int8_ops": ops,
+                             "tops_fused": ops / (ms_bf * 1e-3) / 1e12}
     return out
 
 

@@ -499,9 +499,14 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
     if residual is not None:
         if swiglu or out_ptrs is not None or out_chunks:
             raise ValueError("a residual goes with one plain [M, N] output")
-        res = residual.reshape(M, N).to(torch.bfloat16)
-        res = res if (res.stride(1) == 1 and res.stride(0) % 8 == 0 and res.data_ptr() % 16 == 0) else res.contiguous()
-        g = None if gate is None else gate.reshape(-1, N).to(torch.bfloat16).contiguous()
+        ldp = -(-N // 8) * 8  # bf16 rows the epilogue reads must start on 16-byte boundaries
+
+        def rows16(t: Tensor) -> Tensor:
+            ok = t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+            return t if ok else _pad_cols(t, ldp)
+
+        res = rows16(residual.reshape(M, N).to(torch.bfloat16))
+        g = None if gate is None else rows16(gate.reshape(-1, N).to(torch.bfloat16))
         gi = None
         if gate_index is not None:
             gi = gate_index.reshape(-1).to(device=a.device, dtype=torch.int32).contiguous()
@@ -512,7 +517,8 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         rc = _lib.lib().convrot_gemm_residual(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
                                               _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
                                               up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(res),
-                                              res.stride(0), _ptr(g), N, _ptr(gi), _ptr(y), ldy, _stream(a))
+                                              res.stride(0), _ptr(g), g.stride(0) if g is not None else 0, _ptr(gi),
+                                              _ptr(y), ldy, _stream(a))
         _lib.check(rc, "convrot_gemm_residual")
         return y if ldy == N else y[:, :N]
     if swiglu:
