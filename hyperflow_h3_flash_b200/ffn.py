@@ -21,7 +21,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-from .int8 import _MIN_KERNEL_ROWS, Int8RotLinear, _kernels
+from .int8 import _MIN_KERNEL_ROWS, Int8RotLinear, _kernels, _rows
 
 
 def interleave_rows(n: int, gate_first: bool = False) -> Tensor:
@@ -67,7 +67,7 @@ class SwiGLUInt8(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         proj = self.proj
         shape = x.shape
-        x2 = x.reshape(-1, proj.in_features).to(torch.bfloat16).contiguous()
+        x2 = _rows(x, proj.in_features)
         if not x2.is_cuda:
             return swiglu_reference(proj(x), self.gate_first)
         kernels = _kernels()

@@ -180,7 +180,7 @@ class Int8RotLinear(nn.Module):
                     y = rows[0] * y
             return residual + y
         shape = x.shape
-        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
+        x2 = _rows(x, self.in_features)
         if x2.is_cuda:
             kernels = _kernels()
             if x2.shape[0] >= _MIN_KERNEL_ROWS:
@@ -226,7 +226,7 @@ class Int8RotLinear(nn.Module):
         """The layer with its output written as column chunks to device addresses (CUDA only): chunk j of each row
         to ``out_ptrs[j]`` (``[M, out_ld]`` rows) -- the seq -> head exchange done by the GEMM, when the addresses are
         the other GPUs' receive buffers."""
-        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16).contiguous()
+        x2 = _rows(x, self.in_features)
         if not x2.is_cuda:
             raise ValueError("forward_scatter runs on CUDA tensors only")
         kernels = _kernels()
@@ -315,6 +315,13 @@ def _padded_k(K: int) -> int:
     return -(-K // 16) * 16
 
 
+def _rows(x: Tensor, k: int) -> Tensor:
+    """``x`` as bf16 rows ``[M, k]``, copied only when its last dimension is not unit-stride: a strided row view (a
+    column slice of a wider tensor, e.g. the v part of a fused QKV output) goes to the kernels as it is."""
+    x2 = x.reshape(-1, k).to(torch.bfloat16)
+    return x2 if x2.stride(-1) == 1 else x2.contiguous()
+
+
 def _pad_cols(t: Tensor, cols: int) -> Tensor:
     if t.shape[1] == cols and t.stride(0) % 16 == 0 and t.data_ptr() % 16 == 0:
         return t
@@ -330,7 +337,7 @@ def rotate_quant(x: Tensor, group: int, rounding: int = _lib.ROUND_KERNEL) -> tu
     if K % group:
         raise ValueError(f"K = {K} is not a multiple of the Hadamard group {group}")
     Kp = _padded_k(K)
-    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(0) % 8 or x.data_ptr() % 16) else x
+    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16) else x
     q = torch.empty(M, Kp, dtype=torch.int8, device=x.device)
     s = torch.empty(M, dtype=torch.float32, device=x.device)
     rc = _lib.lib().convrot_rotate_quant(_ptr(xs), xs.stride(0), M, Kp, group, rounding, _ptr(q), Kp, _ptr(s),
@@ -444,7 +451,7 @@ def lowrank_down(x: Tensor, down: Tensor) -> Tensor:
     if down.shape[1] != K:
         raise ValueError(f"down is {tuple(down.shape)}, expected [r, {K}]")
     Kp = -(-K // 8) * 8
-    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(0) % 8 or x.data_ptr() % 16) else x
+    xs = _pad_cols(x, Kp) if (Kp != K or x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16) else x
     ds = _pad_cols(down.contiguous(), Kp) if (Kp != K or down.data_ptr() % 16) else down.contiguous()
     ld = -(-r // 8) * 8
     xa = torch.empty(M, ld, dtype=torch.bfloat16, device=x.device)

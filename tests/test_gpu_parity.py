@@ -654,3 +654,19 @@ def test_gated_residual_in_place_through_the_c_abi():
                                           P(buf.data_ptr()), N, P(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "convrot_gemm_residual")
     assert torch.equal(buf, expected)
+
+
+def test_strided_row_views_go_to_the_kernels_uncopied_and_give_the_same_result():
+    """A column slice of a wider tensor (v of a fused QKV output) is a strided row view: the layer reads it in place
+    (row pitch passed to the kernels) and gives the bits of its contiguous copy; a transposed view is copied."""
+    K, N, M = 1024, 512, 300
+    w = synthetic.linear_weights(K, N, rank=32, bias=True, group=256, seed_offset=50)
+    layer = I.Int8RotLinear(K, N, 256, bias=True, rank=32)
+    synthetic.load_into(layer, w)
+    layer = layer.to(DEV)
+    wide = synthetic.activations(M, 3 * K, seed=97).to(DEV)
+    view = wide[:, 2 * K:]
+    assert view.stride() == (3 * K, 1)
+    assert torch.equal(layer(view), layer(view.contiguous()))
+    tr = view.contiguous().t().contiguous().t()  # same values, column-major
+    assert torch.equal(layer(tr), layer(view.contiguous()))
