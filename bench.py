@@ -2,8 +2,9 @@
 
 Step (every N): the config-2 linear set of one attention block on this rank's tokens -- q, k, v and out convrot
 linears, K = N = 5120, rank-32 low-rank correction and bias, q/k/v sharing one quantisation -- with, for N > 1, the
-Ulysses seq<->head all-to-all of q, k, v ([M/P, 40 heads, 128] bf16) around an identity attention (o = v) and back.
-M = 32768 token rows per rank (weak scaling; N = 4 is BASELINE config 4's 131072 tokens).
+Ulysses seq<->head exchange of q, k, v ([M/P, 40 heads, 128] bf16) around an identity attention (o = v) and back,
+fused into the kernels over peer memory (``--transport peer``, the default) or as NCCL all-to-alls (``nccl``).
+M = 32768 token rows per rank (weak scaling; N = 4 is config 4's 131072 tokens; ``--rows`` changes it).
 
   value       INT8 TOPS of the whole job (4 GEMMs x 2*M*K*N per rank, all ranks) over the device-timed steps
   e2e         the same metric through the public module API with host buffers: each step copies x from pinned
@@ -11,7 +12,8 @@ M = 32768 token rows per rank (weak scaling; N = 4 is BASELINE config 4's 131072
               copies run on their own streams, double-buffered, overlapping the neighbouring steps' compute
   roofline    the tcgen05 GEMM (dominant kernel): 2*M*N*K INT8 ops per launch over its CUDA-event duration in the
               timed region, against the INT8 peak measured here (torch._int_mm = cuBLASLt, 8192^3)
-  extras      (N = 1) config 2's single linear (TOPS), config 3's DiT-block linear set (ms), rotate+quantise GB/s
+  extras      (N = 1) config 2's single linear (TOPS), config 3's DiT-block linear set (ms), its FFN chain with and
+              without the fused SwiGLU, its AdaLN prologue, the whole block fused and unfused, rotate+quantise GB/s
   cpu_baseline the reference's CPU path (_forward_torch, int8.py:173-179) as ported in oracle/ (numpy/BLAS),
               on a bounded row sample, rank 0 at N = 1
 

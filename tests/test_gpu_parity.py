@@ -264,7 +264,7 @@ def test_q_k_v_share_one_quantization(monkeypatch):
 
 @pytest.mark.parametrize("M,K,N", [(32768, 5120, 5120), (32761, 5120, 5120)])
 def test_full_size_sampled_rows_are_bitwise_the_oracle(M, K, N, gemm_mode):
-    """BASELINE configs 2 and 5 (ragged tail): every output row is computed, sampled rows checked bit-exact."""
+    """Configs 2 and 5 (M = 32761: a ragged tail): every output row is computed, sampled rows checked bit-exact."""
     G = 256
     x = synthetic.activations(M, K, seed=0)
     w = synthetic.linear_weights(K, N, bias=False, group=G)
