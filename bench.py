@@ -171,6 +171,24 @@ def cpu_port_linear_set(rows: int, steps: int, warmup: int) -> dict:
             "seconds_per_step": t, "mean_seconds_per_step": statistics.mean(times)}
 
 
+METRIC = "INT8 convrot linear-set TOPS (q,k,v,out; K=N=5120, r=32)"
+DATA = "synthetic (seeded, random-init weights)"
+
+
+def workload_config(rows: int, world: int, transport: str) -> dict:
+    """The `config` object of both arms' lines (the reference arm times a row sample of this same workload)."""
+    exchange = world > 1 and transport == "peer"
+    return {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
+                        f"M={rows} rows/rank, K=N={K_DIM}, r={RANK}, bias, group {GROUP}"
+                        + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity attention"
+                           + (" (fused into the kernels over peer memory)" if exchange else " (NCCL)")
+                           if world > 1 else ""),
+            "rows_per_rank": rows, "total_rows": rows * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
+            "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
+            "transport": transport if world > 1 else None,
+            "l2": "inputs larger than L2 (x is 335 MB per step), no flush"}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -178,12 +196,11 @@ def run_reference(args) -> None:
     rows = 1024
     res = cpu_port_linear_set(rows, args.steps, args.warmup)
     line = {
-        "metric": "INT8 convrot linear-set TOPS (q,k,v,out; K=N=5120, r=32)", "value": res["value"],
+        "metric": METRIC, "value": res["value"],
         "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)", "impl": "reference",
-        "config": {"workload": "config-2 linear set, CPU sample", "rows_sampled": rows, "K": K_DIM, "N": N_DIM,
-                   "rank": RANK, "group": GROUP},
+        "vs_baseline": None, "dtype": "int8", "data": DATA, "impl": "reference",
+        "config": workload_config(args.rows, args.gpus, args.transport),
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -406,19 +423,11 @@ def run_ours(args) -> None:
             cpu = cpu_port_linear_set(2048, 3, 1)
             cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         line = {
-            "metric": "INT8 convrot linear-set TOPS (q,k,v,out; K=N=5120, r=32)",
+            "metric": METRIC,
             "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, random-init weights)",
-            "config": {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
-                                   f"M={M} rows/rank, K=N={K_DIM}, r={RANK}, bias, group {GROUP}"
-                                   + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity "
-                                      "attention" + (" (fused into the kernels over peer memory)"
-                                                     if exchange else " (NCCL)") if world > 1 else ""),
-                       "rows_per_rank": M, "total_rows": M * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
-                       "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
-                       "transport": (args.transport if world > 1 else None),
-                       "l2": "inputs larger than L2 (x is 335 MB per step), no flush"},
+            "vs_baseline": None, "dtype": "int8", "data": DATA,
+            "config": workload_config(M, world, args.transport),
             "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2,
                     "pipelining": "H2D / compute / D2H on three streams, double-buffered"},
