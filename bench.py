@@ -459,7 +459,6 @@ def pipelined_e2e(torch, dev, step, x_host, y_host, args, barrier) -> float:
     y_dev = [None, None]
     uploaded = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(2)]
-    downloaded = [torch.cuda.Event() for _ in range(2)]
 
     def run(n):
         for i in range(n):
@@ -470,15 +469,14 @@ def pipelined_e2e(torch, dev, step, x_host, y_host, args, barrier) -> float:
                 x_dev[b].copy_(x_host, non_blocking=True)
                 uploaded[b].record(up)
             compute.wait_event(uploaded[b])
-            if i >= 2:
-                compute.wait_event(downloaded[b])  # step i-2's output has left y_dev[b]
+            # (each step writes a fresh output tensor; record_stream below keeps the allocator from reusing one
+            # before its download ends, so compute never waits for the download of an earlier step)
             y_dev[b] = step(x_dev[b])
             computed[b].record(compute)
             with torch.cuda.stream(down):
                 down.wait_event(computed[b])
                 y_pin[b].copy_(y_dev[b], non_blocking=True)
                 y_dev[b].record_stream(down)  # the allocator must not recycle it before the download ends
-                downloaded[b].record(down)
         compute.wait_stream(down)
         compute.wait_stream(up)
 
