@@ -775,15 +775,15 @@ int convrot_ipc_close(void* base) {
 
 int convrot_peer_signal(uint32_t* const* slots, int n, uint32_t epoch, void* stream) {
   if (n < 1 || n > kMaxChunks || !slots) return CONVROT_ERR_ARG;
-  DeviceState* st = nullptr;
-  int rc = device_state(&st);
-  if (rc) return rc;
   PeerSlots ps;
   memset(&ps, 0, sizeof(ps));
   for (int j = 0; j < n; ++j) {
     if (!slots[j] || (reinterpret_cast<uintptr_t>(slots[j]) & 3u)) return CONVROT_ERR_ARG;
     ps.slot[j] = slots[j];
   }
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
   peer_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ps, n, epoch);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);

@@ -91,3 +91,54 @@ def test_status_mapping_to_exceptions(lib):
     with pytest.raises(lib.ConvrotError):
         lib.check(lib.ERR_TIMEOUT, "x")
     lib.check(lib.OK, "x")
+
+
+def test_fused_and_exchange_entry_points_reject_bad_arguments(lib):
+    """The SwiGLU, gated-residual, AdaLN, scatter / gather and peer entry points check their arguments first."""
+    L = lib.lib()
+    p = ctypes.c_void_p(4096)
+    P = ctypes.c_void_p
+    # SwiGLU: N must split into 64-column a/g block pairs
+    assert L.convrot_gemm_swiglu(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 96, 64, p, 48, None) == \
+        lib.ERR_SHAPE
+    # gated residual: residual rows narrower than N, a misaligned pitch, no residual at all
+    assert L.convrot_gemm_residual(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 64, 64, p, 32, None, 0,
+                                   None, p, 64, None) == lib.ERR_SHAPE
+    assert L.convrot_gemm_residual(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 64, 64, p, 68, None, 0,
+                                   None, p, 64, None) == lib.ERR_ALIGN
+    assert L.convrot_gemm_residual(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 64, 64, None, 64, None, 0,
+                                   None, p, 64, None) == lib.ERR_ARG
+    # AdaLN prologue: group 256 only, K a multiple of 256 up to 8192, a finite non-negative eps
+    args = dict(x=p, ldx=512, M=4, K=512, group=256, rounding=0, sc=p, sh=p, idx=p, ldm=512, eps=1e-6, q=p, ldq=512,
+                s=p, h=None, ldh=0)
+
+    def adaln(**kw):
+        a = {**args, **kw}
+        return L.convrot_rotate_quant_adaln(a["x"], a["ldx"], a["M"], a["K"], a["group"], a["rounding"], a["sc"],
+                                            a["sh"], a["idx"], a["ldm"], a["eps"], a["q"], a["ldq"], a["s"], a["h"],
+                                            a["ldh"], None)
+
+    assert adaln(group=64) == lib.ERR_GROUP
+    assert adaln(K=640, ldx=640, ldq=640, ldm=640) == lib.ERR_SHAPE
+    assert adaln(K=8448, ldx=8448, ldq=8448, ldm=8448) == lib.ERR_SHAPE
+    assert adaln(eps=-1.0) == lib.ERR_ARG
+    assert adaln(eps=float("nan")) == lib.ERR_ARG
+    assert adaln(sc=None) == lib.ERR_ARG
+    assert adaln(M=0) == lib.OK
+    # scatter / gather: at least two and at most eight chunks, chunk widths the kernels can address
+    outs = (P * 9)(*([4096] * 9))
+    assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 256, 64, outs, 1, 128,
+                                  None) == lib.ERR_ARG
+    assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 288, 64, outs, 9, 32,
+                                  None) == lib.ERR_ARG
+    assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 96, 64, outs, 2, 48,
+                                  None) == lib.ERR_SHAPE  # 48-column chunks
+    assert L.convrot_rotate_quant_gather(outs, 2, 192, 4, 384, 256, 0, p, 384, p, None, 0, None) == lib.ERR_SHAPE
+    assert L.convrot_rotate_quant_gather(outs, 1, 512, 4, 512, 256, 0, p, 512, p, None, 0, None) == lib.ERR_ARG
+    # peer signalling: at most eight ranks, word-aligned flags
+    slots = (P * 2)(4096, 4098)
+    assert L.convrot_peer_signal(slots, 2, 1, None) == lib.ERR_ARG
+    assert L.convrot_peer_signal(slots, 9, 1, None) == lib.ERR_ARG
+    assert L.convrot_peer_wait(P(4098), 2, 1, None) == lib.ERR_ARG
+    assert L.convrot_ipc_open(None, None) == lib.ERR_ARG
+    assert L.convrot_ipc_close(None) == lib.ERR_ARG
