@@ -409,10 +409,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       auto try_lr = [&]() {
         if (!HAS_LR || pending_lr < 0) return;
         if (!lr_epi_seen) {
-          if (!mbar_try_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+          if (!mbar_test_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
           lr_epi_seen = true;
         }
-        if (!mbar_try_wait(lr_full, lr_full_phase)) return;
+        if (!mbar_test_wait(lr_full, lr_full_phase)) return;
         lr_step();
       };
       auto flush_lr = [&]() -> bool {

@@ -54,6 +54,19 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return done != 0;
 }
 
+// Non-blocking cluster-scope check (see mbar_test_wait).
+__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Bounded wait with cluster-scope acquire, for barriers that receive arrivals from the other CTA.
 __device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns,
                                                           volatile int* abort) {
@@ -312,10 +325,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       auto try_lr = [&]() {
         if (!HAS_LR || pending_lr < 0) return;
         if (!lr_epi_seen) {
-          if (!mbar_try_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+          if (!mbar_test_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
           lr_epi_seen = true;
         }
-        if (!mbar_try_wait(lr_full, lr_full_phase)) return;
+        if (!mbar_test_wait(lr_full, lr_full_phase)) return;
         lr_step();
       };
       auto flush_lr = [&]() -> bool {
