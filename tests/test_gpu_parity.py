@@ -670,3 +670,23 @@ def test_strided_row_views_go_to_the_kernels_uncopied_and_give_the_same_result()
     assert torch.equal(layer(view), layer(view.contiguous()))
     tr = view.contiguous().t().contiguous().t()  # same values, column-major
     assert torch.equal(layer(tr), layer(view.contiguous()))
+
+
+def test_zero_padded_rank_gives_the_same_output():
+    """The reference pads low-rank ranks with zero rows of down and zero columns of up at load
+    (transformer.py:60-72, 205-216); the fused term over the padded rank is bitwise the unpadded one."""
+    K, N, M, r = 1024, 512, 300, 40
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256, seed_offset=60)
+    small = I.Int8RotLinear(K, N, 256, bias=True, rank=r)
+    synthetic.load_into(small, w)
+    padded = I.Int8RotLinear(K, N, 256, bias=True, rank=64)
+    with torch.no_grad():
+        padded.qweight.copy_(small.qweight)
+        padded.wscale.copy_(small.wscale)
+        padded.bias.copy_(small.bias)
+        padded.down.weight.zero_()
+        padded.up.weight.zero_()
+        padded.down.weight[:r].copy_(small.down.weight)
+        padded.up.weight[:, :r].copy_(small.up.weight)
+    x = synthetic.activations(M, K, seed=98).to(DEV)
+    assert torch.equal(small.to(DEV)(x), padded.to(DEV)(x))

@@ -157,3 +157,25 @@ def test_gated_residual_on_cpu_is_the_bf16_composition():
     assert torch.equal(layer(x, residual=res, gate=gate, gate_index=idx), res + gate.index_select(0, idx) * y)
     assert torch.equal(layer(x, residual=res, gate=gate[1]), res + gate[1] * y)
     assert torch.equal(layer(x, residual=res), res + y)
+
+
+def test_save_and_load_keep_storage_dtypes_and_outputs(tmp_path):
+    """tests/test_transformer.py:164-175 on this layer: a saved state dict reloads with int8 / fp32 / bf16 storage
+    and the same outputs."""
+    import torch
+
+    from hyperflow_h3_flash_b200 import int8 as I
+    from hyperflow_h3_flash_b200 import synthetic
+
+    w = synthetic.linear_weights(256, 128, rank=16, bias=True, group=64)
+    layer = I.Int8RotLinear(256, 128, 64, bias=True, rank=16)
+    synthetic.load_into(layer, w)
+    path = tmp_path / "layer.pt"
+    torch.save(layer.state_dict(), path)
+    fresh = I.Int8RotLinear(256, 128, 64, bias=True, rank=16)
+    fresh.load_state_dict(torch.load(path))
+    dtypes = {k: v.dtype for k, v in fresh.state_dict().items()}
+    assert dtypes == {"qweight": torch.int8, "wscale": torch.float32, "bias": torch.bfloat16,
+                      "down.weight": torch.bfloat16, "up.weight": torch.bfloat16}
+    x = synthetic.activations(20, 256, seed=5)
+    assert torch.equal(fresh(x), layer(x))
