@@ -52,7 +52,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
-    ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "down"], default=None,
+    ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "down"],
+                    default=None,
                     help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
     return ap.parse_args()
 
@@ -660,7 +661,13 @@ def run_case(args) -> None:
         perm = ffn.interleave_rows(2 * 13824)
         wf = synthetic.LinearWeights(wf.qweight[perm], wf.wscale[perm], wf.bias[perm], wf.down, wf.up[perm]).to(dev)
         xa64 = I.lowrank_down(x, wf.down)
+    if args.case == "rotate_adaln":  # the AdaLN prologue of a block: 8 modulation rows, frames of tokens
+        gen = torch.Generator().manual_seed(9)
+        mod_sc = (torch.randn(8, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
+        mod_sh = (torch.randn(8, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
+        mod_idx = (torch.arange(M, device=dev) * 8 // M).to(torch.int32)
     fns = {
+        "rotate_adaln": lambda: I.rotate_quant_adaln(x, GROUP, mod_sc, mod_sh, mod_idx),
         "gemm_ffn_up": lambda: I.convrot_matmul(q, wf.qweight, s, wf.wscale, bias=wf.bias, xa=xa64, up=wf.up,
                                                 swiglu=True),
         "gemm": lambda: I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up),

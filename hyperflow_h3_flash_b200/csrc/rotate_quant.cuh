@@ -354,21 +354,21 @@ __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stage
 
 // AdaLN on a pair of bf16 values (low half = even column): n = bf16((x - mean) * rstd) in fp32, then
 // bf16(bf16(n * bf16(1 + scale)) + shift), each step rounded to bf16 as the unfused bf16 tensor ops round it.
+// Two fp32 values rounded to bf16 in one paired conversion, returned as the packed pair and unpacked again.
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t p) { return __uint_as_float(p << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t p) { return __uint_as_float(p & 0xffff0000u); }
+
 __device__ __forceinline__ uint32_t adaln_pair(uint32_t w, uint32_t sc, uint32_t sh, float mean, float rstd) {
-  uint32_t out = 0;
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int shift = 16 * half;
-    const float x = __uint_as_float(((w >> shift) & 0xffffu) << 16);
-    const float s = __uint_as_float(((sc >> shift) & 0xffffu) << 16);
-    const float b = __uint_as_float(((sh >> shift) & 0xffffu) << 16);
-    const float n = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fsub_rn(x, mean), rstd)));
-    const float one_s = __bfloat162float(__float2bfloat16_rn(__fadd_rn(1.0f, s)));
-    const float t = __bfloat162float(__float2bfloat16_rn(__fmul_rn(n, one_s)));
-    const __nv_bfloat16 h = __float2bfloat16_rn(__fadd_rn(t, b));
-    out |= static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&h)) << shift;
-  }
-  return out;
+  // both halves step by step, each rounding done on the pair at once
+  const uint32_t n = bf16x2_rn(__fmul_rn(__fsub_rn(bf16_lo(w), mean), rstd),
+                               __fmul_rn(__fsub_rn(bf16_hi(w), mean), rstd));
+  const uint32_t one_s = bf16x2_rn(__fadd_rn(1.0f, bf16_lo(sc)), __fadd_rn(1.0f, bf16_hi(sc)));
+  const uint32_t t = bf16x2_rn(__fmul_rn(bf16_lo(n), bf16_lo(one_s)), __fmul_rn(bf16_hi(n), bf16_hi(one_s)));
+  return bf16x2_rn(__fadd_rn(bf16_lo(t), bf16_lo(sh)), __fadd_rn(bf16_hi(t), bf16_hi(sh)));
 }
 
 // CHUNKED selects the chunked-row input (the Ulysses layouts, in this GPU's memory or gathered from the others'):
