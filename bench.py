@@ -645,6 +645,30 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         n = I.adaln_modulate_quantize(h2, scale_mlp, shift_mlp, mod_idx, GROUP)
         return layers["ffn_down"](swiglu_up(n), residual=h2, gate=gate_mlp, gate_index=mod_idx)
 
+    # config 5: cross-attention K/V projections on text tokens (4096 -> 5120, r = 32), eager and as a CUDA graph
+    from hyperflow_h3_flash_b200.graphs import CapturedCall
+
+    kv_layers = []
+    for i in range(2):
+        wl = synthetic.linear_weights(4096, K_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=80 + i)
+        ly = I.Int8RotLinear(4096, K_DIM, GROUP, bias=True, rank=RANK)
+        synthetic.load_into(ly, wl)
+        kv_layers.append(ly.to(dev))
+    kv_layers[0].keep_input = True
+
+    def kv(t):
+        return kv_layers[0](t), kv_layers[1](t)
+
+    cfg5 = {}
+    for rows in (256, 333):
+        xt = synthetic.activations(rows, 4096, seed=rows).to(dev)
+        graphed = CapturedCall(kv, xt)
+        cfg5[f"M{rows}"] = {"eager_us": timed(lambda: kv(xt), args.steps * 5) * 1e3,
+                            "graph_us": timed(lambda: graphed(xt), args.steps * 5) * 1e3}
+    out["cross_attention_kv_cfg5"] = {"config": "config 5: K and V projections 4096 -> 5120 (r=32, bias, shared "
+                                                "quantisation) on 256 / 333 text tokens, per call",
+                                      **cfg5}
+
     ms_bu = timed(block_unfused, max(3, args.steps // 2))
     ms_bf = timed(block_fused, max(3, args.steps // 2))
     out["dit_block_cfg3"] = {"config": "config 3 block dataflow (chunk_block with identity attention): AdaLN, QKV, "

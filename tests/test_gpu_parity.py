@@ -690,3 +690,30 @@ def test_zero_padded_rank_gives_the_same_output():
         padded.up.weight[:, :r].copy_(small.up.weight)
     x = synthetic.activations(M, K, seed=98).to(DEV)
     assert torch.equal(small.to(DEV)(x), padded.to(DEV)(x))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 4096, 5120), (333, 4096, 5120)])
+def test_captured_graph_replays_the_layer_bitwise(M, K, N):
+    """Config 5's cross-attention K/V projection captured once into a CUDA graph: replays on new inputs equal the
+    eager layer bit for bit (and the two projections share one quantisation inside the graph)."""
+    from hyperflow_h3_flash_b200.graphs import CapturedCall
+
+    def layer(seed):
+        w = synthetic.linear_weights(K, N, rank=32, bias=True, group=256, seed_offset=seed)
+        m = I.Int8RotLinear(K, N, 256, bias=True, rank=32)
+        synthetic.load_into(m, w)
+        return m.to(DEV)
+
+    to_k, to_v = layer(70), layer(71)
+    to_k.keep_input = True
+
+    def kv(x):
+        return to_k(x), to_v(x)
+
+    x0 = synthetic.activations(M, K, seed=99).to(DEV)
+    graphed = CapturedCall(kv, x0)
+    for seed in (100, 101):
+        x = synthetic.activations(M, K, seed=seed).to(DEV)
+        k_g, v_g = graphed(x)
+        k_e, v_e = kv(x)
+        assert torch.equal(k_g, k_e) and torch.equal(v_g, v_e)
