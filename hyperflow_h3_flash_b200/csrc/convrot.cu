@@ -409,12 +409,35 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
   int threads = (nslots + slots - 1) / slots;
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
-  // Resident CTAs first (registers ~64 per thread), then the deepest row ring that fits beside them; the grid
-  // is oversubscribed 4x so that the last rows spread evenly (measured on B200 for K = 13824).
-  const int regs_per_thread = slots == 1 ? 64 : 128;
-  int resident = 65536 / (threads * regs_per_thread);
+  cudaError_t e;
+  void (*kernel)(const RotQuantParams) = nullptr;
+  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
+  switch (slots) {
+    case 1: kernel = torch_rounding ? rotate_quant_kernel<G, 1, 1> : rotate_quant_kernel<G, 1, 0>; break;
+    case 2: kernel = torch_rounding ? rotate_quant_kernel<G, 2, 1> : rotate_quant_kernel<G, 2, 0>; break;
+    default: kernel = torch_rounding ? rotate_quant_kernel<G, 4, 1> : rotate_quant_kernel<G, 4, 0>; break;
+  }
+  int regs = -1;  // the kernel's registers per thread, cached with the shared-memory opt-in
+  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &regs);
+  if (rc) return rc;
+  if (regs < 0) {
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
+      return cuda_fail(e);
+    cudaFuncAttributes attr;
+    if ((e = cudaFuncGetAttributes(&attr, kernel)) != cudaSuccess) return cuda_fail(e);
+    regs = attr.numRegs > 0 ? attr.numRegs : 128;
+    store_resident(reinterpret_cast<const void*>(kernel), regs);
+  }
+  // Resident CTAs first (from the kernel's registers, allocated per warp in units of 8 per thread), then the
+  // deepest row ring that fits beside them: the per-row chain is latency-bound, so CTAs beat ring depth (measured
+  // on B200 for K = 13824: 2 CTAs x 1 row buffer 0.57 ms, 1 CTA x 6 buffers 0.69 ms).  The grid is
+  // oversubscribed 4x so that the last rows spread evenly.
+  const int regs_alloc = (regs + 7) / 8 * 8;
+  int resident = 65536 / (threads * regs_alloc);
   if (resident > 2048 / threads) resident = 2048 / threads;
   if (resident < 1) resident = 1;
+  while (resident > 1 && static_cast<size_t>(resident) * (rq_smem_bytes(p.K, threads, 1) + 1024) > 228 * 1024)
+    --resident;
   int stages = 1;
   for (int st_try = 2; st_try <= kRQMaxStages; ++st_try) {
     const size_t sm = rq_smem_bytes(p.K, threads, st_try);
@@ -427,23 +450,6 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
   q.stages = stages;
   const size_t smem = rq_smem_bytes(p.K, threads, stages);
   if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
-  cudaError_t e;
-  void (*kernel)(const RotQuantParams) = nullptr;
-  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
-  switch (slots) {
-    case 1: kernel = torch_rounding ? rotate_quant_kernel<G, 1, 1> : rotate_quant_kernel<G, 1, 0>; break;
-    case 2: kernel = torch_rounding ? rotate_quant_kernel<G, 2, 1> : rotate_quant_kernel<G, 2, 0>; break;
-    default: kernel = torch_rounding ? rotate_quant_kernel<G, 4, 1> : rotate_quant_kernel<G, 4, 0>; break;
-  }
-  // The opt-in covers the largest configuration once; residency depends on (threads, smem), i.e. on K.
-  int opted = -1;
-  int rc = cached_resident(reinterpret_cast<const void*>(kernel), &opted);
-  if (rc) return rc;
-  if (opted < 0) {
-    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)) != cudaSuccess)
-      return cuda_fail(e);
-    store_resident(reinterpret_cast<const void*>(kernel), 1);
-  }
   int64_t grid = static_cast<int64_t>(st.sms) * best_blocks;
   if (grid > p.M) grid = p.M;
   kernel<<<static_cast<int>(grid), threads, smem, stream>>>(q);
