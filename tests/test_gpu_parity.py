@@ -80,6 +80,8 @@ def gemm_mode(request):
 @pytest.mark.parametrize("M,K,group", [
     (1, 256, 256), (17, 1024, 256), (70, 1024, 256), (333, 4096, 256), (64, 5120, 256), (40, 13824, 256),
     (33, 512, 16), (33, 1024, 64), (33, 64, 4), (5, 16384, 256), (3, 32768, 256), (129, 2048, 16),
+    # more rows than CTAs: each CTA cycles its row ring several times (a one-buffer ring at K = 13824)
+    (4000, 13824, 256), (4000, 13824, 16), (2500, 16384, 256), (5000, 5120, 256),
 ])
 def test_rotate_quant_is_bitwise_the_oracle(M, K, group, rotate_variant):
     x = edge_rows(synthetic.activations(M, K, seed=M + K), group)
