@@ -539,6 +539,17 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         e.synchronize()
         return s.elapsed_time(e) / steps
 
+    def timed_ab(fns: dict, steps: int, rounds: int = 4) -> dict:
+        """Per-call ms of each variant, median over rounds that alternate the variants (order reversed every
+        other round). Seconds of INT8 GEMMs push the GPU onto its 1 kW power cap and its clock drifts down; timing
+        one variant after the other would charge the drift to the later one."""
+        names = list(fns)
+        samples = {n: [] for n in names}
+        for r in range(rounds):
+            for n in (names if r % 2 == 0 else names[::-1]):
+                samples[n].append(timed(fns[n], steps))
+        return {n: sorted(v)[len(v) // 2] for n, v in samples.items()}
+
     M = args.rows
     w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=7)
     layer = I.Int8RotLinear(K_DIM, N_DIM, GROUP, bias=True, rank=RANK)
@@ -569,11 +580,7 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         layers["ffn_up"](xb)
         layers["ffn_down"](hb)
 
-    ms = timed(block, max(3, args.steps // 2))
     ops = sum(2.0 * Mb * K * N for _, K, N in shapes)
-    out["block_set_cfg3"] = {"config": "config 3: M=32760, r=64, QKV 5120->15360, out 5120->5120, "
-                                       "FFN-up 5120->27648, FFN-down 13824->5120 (bias, low-rank)",
-                             "ms": ms, "tops": ops / (ms * 1e-3) / 1e12}
 
     # the same block with the feed-forward's real dataflow: FFN-down reads the SwiGLU of FFN-up's output, either
     # unfused (projection [M, 27648] -> a * silu(g) in torch -> down) or fused into the FFN-up epilogue
@@ -592,9 +599,14 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         layers["out"](xb)
         chain_fused()
 
-    ms_unfused = timed(chain_unfused, max(3, args.steps // 2))
-    ms_fused = timed(chain_fused, max(3, args.steps // 2))
-    ms_block = timed(block_fused, max(3, args.steps // 2))
+    steps_b = max(3, args.steps // 4)
+    t = timed_ab({"block": block, "block_fused": block_fused}, steps_b)
+    ms, ms_block = t["block"], t["block_fused"]
+    out["block_set_cfg3"] = {"config": "config 3: M=32760, r=64, QKV 5120->15360, out 5120->5120, "
+                                       "FFN-up 5120->27648, FFN-down 13824->5120 (bias, low-rank)",
+                             "ms": ms, "tops": ops / (ms * 1e-3) / 1e12}
+    t = timed_ab({"unfused": chain_unfused, "fused": chain_fused}, steps_b)
+    ms_unfused, ms_fused = t["unfused"], t["fused"]
     out["ffn_chain_cfg3"] = {"config": "M=32760: FFN-up 5120->27648 (r=64, bias) -> a*silu(g) -> FFN-down "
                                        "13824->5120 (r=64, bias)",
                              "ms_unfused": ms_unfused, "ms_fused_swiglu": ms_fused}
@@ -619,8 +631,8 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         return I.rotate_quant_adaln(xb, GROUP, mod_scale, mod_shift, mod_idx)
 
     out["adaln_prologue_cfg3"] = {"config": "M=32760, K=5120, 8 modulation rows: LayerNorm + modulate + rotate+quantise",
-                                  "ms_unfused": timed(adaln_unfused, args.steps),
-                                  "ms_fused": timed(adaln_fused, args.steps)}
+                                  **{f"ms_{k}": v for k, v in timed_ab({"unfused": adaln_unfused,
+                                                                        "fused": adaln_fused}, args.steps).items()}}
 
     # the whole block as chunk_block runs it (transformer.py:339-380), attention replaced by identity (o = v):
     # AdaLN -> QKV -> out + gated residual -> AdaLN -> FFN-up -> SwiGLU -> FFN-down + gated residual
@@ -663,14 +675,14 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     for rows in (256, 333):
         xt = synthetic.activations(rows, 4096, seed=rows).to(dev)
         graphed = CapturedCall(kv, xt)
-        cfg5[f"M{rows}"] = {"eager_us": timed(lambda: kv(xt), args.steps * 5) * 1e3,
-                            "graph_us": timed(lambda: graphed(xt), args.steps * 5) * 1e3}
+        t = timed_ab({"eager": lambda: kv(xt), "graph": lambda: graphed(xt)}, args.steps * 5)
+        cfg5[f"M{rows}"] = {"eager_us": t["eager"] * 1e3, "graph_us": t["graph"] * 1e3}
     out["cross_attention_kv_cfg5"] = {"config": "config 5: K and V projections 4096 -> 5120 (r=32, bias, shared "
                                                 "quantisation) on 256 / 333 text tokens, per call",
                                       **cfg5}
 
-    ms_bu = timed(block_unfused, max(3, args.steps // 2))
-    ms_bf = timed(block_fused, max(3, args.steps // 2))
+    t = timed_ab({"unfused": block_unfused, "fused": block_fused}, steps_b)
+    ms_bu, ms_bf = t["unfused"], t["fused"]
     out["dit_block_cfg3"] = {"config": "config 3 block dataflow (chunk_block with identity attention): AdaLN, QKV, "
                                        "out + gated residual, AdaLN, FFN-up, SwiGLU, FFN-down + gated residual",
                              "ms_unfused": ms_bu, "ms_fused": ms_bf, "int8_ops": ops,
