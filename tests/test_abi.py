@@ -42,6 +42,11 @@ def test_every_declared_function_is_exported_and_bound(lib):
     assert sorted(lib.SIGNATURES) == names  # the Python binding covers exactly the header
 
 
+def test_integration_guide_names_every_declared_function():
+    guide = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    assert [n for n in declared_functions() if n not in guide] == []
+
+
 def test_status_strings_and_version(lib):
     L = lib.lib()
     for code in range(8):
