@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_gemm_residual": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P, _L, _P, _P, _L,
                                _P], _I),
     "convrot_gemm_swiglu": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
+    "convrot_silu": ([_P, _P, _L, _P], _I),
     "convrot_gemm_scatter": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _I, _L, _P], _I),
     "convrot_rotate_quant_gather": ([_P, _I, _L, _L, _L, _I, _I, _P, _L, _P, _P, _L, _P], _I),
     "convrot_ipc_handle": ([_P, _P, _P], _I),

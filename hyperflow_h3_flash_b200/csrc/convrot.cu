@@ -733,6 +733,22 @@ int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
                  static_cast<cudaStream_t>(stream), nullptr, 1, true);
 }
 
+int convrot_silu(const void* x, void* y, int64_t n, void* stream) {
+  if (n < 0) return CONVROT_ERR_SHAPE;
+  if (n == 0) return CONVROT_OK;
+  if (!x || !y) return CONVROT_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 1) return CONVROT_ERR_ALIGN;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 4 * static_cast<int64_t>(st->sms)) blocks = 4 * static_cast<int64_t>(st->sms);
+  silu_bf16_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), n);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+}
+
 int convrot_gemm_scatter(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
                          const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
                          int64_t M, int64_t N, int64_t K, void* const* y_chunks, int n_chunks, int64_t ldy,

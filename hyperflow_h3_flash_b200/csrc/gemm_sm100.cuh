@@ -230,13 +230,43 @@ __device__ __forceinline__ void gated_residual(float (&t)[32], const GemmParams&
   }
 }
 
+// silu on a bf16 input g: bf16(g / (1 + expf(-g))), the bits torch's F.silu gives a bf16 tensor (fp32 arithmetic,
+// IEEE division).  It depends on the 16 bits of g alone, so a table of it is exact: the 2-SM epilogue reads it from
+// shared memory for the magnitudes [2^-19, 32) of both signs (24 binades of 128 mantissas, filled once per CTA by
+// this same function) and evaluates the function itself for every other input (zeros, tiny or large magnitudes,
+// inf, NaN).
+constexpr uint32_t kSiluExpLo = 108;                    // bf16 exponent field of 2^-19
+constexpr uint32_t kSiluPerSign = 24 * 128;             // table entries per sign
+constexpr int kSiluTableBytes = 2 * kSiluPerSign * 2;   // 12 KB
+
+__device__ __forceinline__ float silu_bf16(float g) {  // g holds a bf16 value
+  return __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
+}
+
+// Entries [first, 2 * kSiluPerSign) in steps of `step`: positive magnitudes first, then negative.
+__device__ __forceinline__ void silu_table_fill(uint16_t* tab, int first, int step) {
+  for (int i = first; i < static_cast<int>(2 * kSiluPerSign); i += step) {
+    const uint32_t sign = i >= static_cast<int>(kSiluPerSign) ? 0x8000u : 0u;
+    const uint32_t bits = sign | ((static_cast<uint32_t>(i) % kSiluPerSign) + (kSiluExpLo << 7));
+    tab[i] = static_cast<uint16_t>(__float_as_uint(silu_bf16(__uint_as_float(bits << 16))) >> 16);
+  }
+}
+
+// silu_bf16 of the bf16 value with bits b (< 2^16), from the table; sets `miss` when b lies outside it.
+__device__ __forceinline__ float silu_lookup(const uint16_t* tab, uint32_t b, bool& miss) {
+  const uint32_t off = (b & 0x7fffu) - (kSiluExpLo << 7);
+  const bool in = off < kSiluPerSign;
+  miss = miss || !in;
+  return __uint_as_float(static_cast<uint32_t>(tab[in ? off + (b >> 15) * kSiluPerSign : 0u]) << 16);
+}
+
 // SwiGLU over the interleaved projection, one 32-column block at a time (c = the block's first column in the tile):
 // an `a` block (c / 32 even) is kept as bf16 in ya; on the `g` block that follows, t becomes the pair's 32 outputs
-//   h = bf16( float(bf16(a)) * float(bf16( g / (1 + exp(-g)) )) ),  g = float(bf16(t)),
-// the bf16 composition that `a * silu(g)` evaluates on the bf16 outputs of the projection (silu in fp32, each result
-// rounded to bf16; the product of two bf16 values is exact in fp32, so the caller's bf16 store rounds it once).
-// Returns whether t holds outputs to store.
-__device__ __forceinline__ bool swiglu_block(float (&t)[32], int c, uint32_t (&ya)[16]) {
+//   h = bf16( float(bf16(a)) * silu_bf16(float(bf16(t))) ),
+// the bf16 composition that `a * silu(g)` evaluates on the bf16 outputs of the projection (the product of two bf16
+// values is exact in fp32, so the caller's bf16 store rounds it once).  `tab` is the silu table in shared memory,
+// or null to evaluate silu_bf16 directly.  Returns whether t holds outputs to store.
+__device__ __forceinline__ bool swiglu_block(float (&t)[32], int c, uint32_t (&ya)[16], const uint16_t* tab) {
   if (((c >> 5) & 1) == 0) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -245,14 +275,42 @@ __device__ __forceinline__ bool swiglu_block(float (&t)[32], int c, uint32_t (&y
     }
     return false;
   }
+  float sg[32];
+  bool miss = tab == nullptr;
+  if (tab) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(t[2 * j], t[2 * j + 1]);
+      const uint32_t gb = *reinterpret_cast<uint32_t*>(&h);
+      sg[2 * j] = silu_lookup(tab, gb & 0xffffu, miss);
+      sg[2 * j + 1] = silu_lookup(tab, gb >> 16, miss);
+    }
+  }
+  if (miss) {  // no table, or an input outside it: the function itself for the whole block
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sg[j] = silu_bf16(__bfloat162float(__float2bfloat16_rn(t[j])));
+  }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const float a = __uint_as_float((j & 1) ? (ya[j >> 1] & 0xffff0000u) : (ya[j >> 1] << 16));
-    const float g = __bfloat162float(__float2bfloat16_rn(t[j]));
-    const float silu = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g)))));
-    t[j] = __fmul_rn(a, silu);
+    t[j] = __fmul_rn(a, sg[j]);
   }
   return true;
+}
+
+// The epilogue's silu alone, elementwise over n bf16 values (convrot_silu): the same table and the same fallback.
+__global__ void __launch_bounds__(256) silu_bf16_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int64_t n) {
+  __shared__ uint16_t tab[2 * kSiluPerSign];
+  silu_table_fill(tab, threadIdx.x, blockDim.x);
+  __syncthreads();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t b = __bfloat16_as_ushort(x[i]);
+    bool miss = false;
+    float v = silu_lookup(tab, b, miss);
+    if (miss) v = silu_bf16(__uint_as_float(b << 16));
+    y[i] = __float2bfloat16_rn(v);
+  }
 }
 
 template <class Cfg, int KIND, int EPI, int LR_ATOM, int LR_ATOMS>
@@ -568,7 +626,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
               if (p.res) gated_residual(t, p, row, n);
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
             }
-          } else if (swiglu_block(t, c, ya) && row_ok) {
+          } else if (swiglu_block(t, c, ya, nullptr) && row_ok) {
             store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n - 32) >> 1), t, (n - 32) >> 1, n_out);
           }
         }
@@ -595,7 +653,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (!p.swiglu) {
               if (p.res) gated_residual(t, p, row, n0 + c);
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
-            } else if (swiglu_block(t, c, ya))
+            } else if (swiglu_block(t, c, ya, nullptr))
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n0 + c - 32) >> 1), t, (n0 + c - 32) >> 1, n_out);
           }
         }

@@ -153,8 +153,10 @@ struct Gemm2Cfg {
   // Output staging: per epilogue warp two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B) for TMA stores.
   static constexpr int kStoreBoxBytes = 32 * 64;
   static constexpr int kStoreBytes = 4 * 2 * kStoreBoxBytes;
+  // After the barriers: the silu table of the SwiGLU epilogue (filled only by SwiGLU launches).
   static constexpr int kSmemBytes =
-      1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kStoreBytes + kBarBytes;
+      1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kStoreBytes + kBarBytes + kSiluTableBytes;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory above the sm_100 per-CTA limit");
   static constexpr uint32_t kIdesc = make_idesc_i8(256, 256);
   static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 256);
 };
@@ -190,6 +192,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* drain = tmem_full + 10;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  uint16_t* silu_tab = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + Cfg::kBarBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -232,8 +235,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     tmem_alloc_pair<Cfg::kTmemCols>(tmem_holder);
     tmem_relinquish_pair();
   }
+  if (p.swiglu) silu_table_fill(silu_tab, threadIdx.x, blockDim.x);
   tc_fence_before();
-  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated for the pair
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated for the pair, the silu table filled
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const uint64_t limit = p.wait_limit_ns;
@@ -502,7 +506,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
           } else if (!p.swiglu) {
             if (p.res && row_ok) gated_residual(t, p, row, n);
             stage_and_store(t, m0 + quad * 32, n);  // rows beyond M are clipped by the TMA store
-          } else if (swiglu_block(t, c, ya)) {
+          } else if (swiglu_block(t, c, ya, silu_tab)) {
             stage_and_store(t, m0 + quad * 32, (n - 32) >> 1);
           }
         }
@@ -527,7 +531,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             if (!p.swiglu) {
               if (p.res && row_ok) gated_residual(t, p, row, n0 + c);
               stage_and_store(t, m0 + quad * 32, n0 + c);
-            } else if (swiglu_block(t, c, ya))
+            } else if (swiglu_block(t, c, ya, silu_tab))
               stage_and_store(t, m0 + quad * 32, (n0 + c - 32) >> 1);
           }
         }

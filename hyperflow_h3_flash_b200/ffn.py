@@ -17,10 +17,13 @@ Which half is the gate comes from diffusers (absent here): ``gate_first=False`` 
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
+from . import _lib
 from .int8 import _MIN_KERNEL_ROWS, Int8RotLinear, _kernels, _rows
 
 
@@ -34,6 +37,20 @@ def interleave_rows(n: int, gate_first: bool = False) -> Tensor:
     a0, g0 = (half, 0) if gate_first else (0, half)
     blocks = torch.arange(half // 32).view(-1, 1) * 32 + torch.arange(32).view(1, -1)  # [half / 32, 32]
     return torch.stack([a0 + blocks, g0 + blocks], dim=1).reshape(n)
+
+
+def silu_bf16(x: Tensor) -> Tensor:
+    """``F.silu`` of a bf16 CUDA tensor computed by the fused SwiGLU epilogue's own silu (its table plus the formula
+    for inputs outside it; ``convrot_silu``).  Same bits as torch's ``F.silu``; exists so that the epilogue's silu can
+    be checked over every bf16 input."""
+    if not x.is_cuda or x.dtype != torch.bfloat16:
+        raise ValueError(f"silu_bf16 takes a bf16 CUDA tensor, got {x.dtype} on {x.device}")
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    _lib.check(_lib.lib().convrot_silu(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()), x.numel(),
+                                       ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)),
+               "convrot_silu")
+    return y
 
 
 def swiglu_reference(y: Tensor, gate_first: bool = False) -> Tensor:
@@ -83,4 +100,4 @@ class SwiGLUInt8(nn.Module):
         return h.reshape(*shape[:-1], self.out_features)
 
 
-__all__ = ["SwiGLUInt8", "interleave_rows", "swiglu_reference"]
+__all__ = ["SwiGLUInt8", "interleave_rows", "silu_bf16", "swiglu_reference"]

@@ -158,6 +158,15 @@ int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
                         int64_t M, int64_t N, int64_t K, void* h, int64_t ldh, void* stream);
 
 /*
+ * The SwiGLU epilogue's silu alone, elementwise: y[i] = bf16( x[i] / (1 + exp(-x[i])) ) over n bf16 values, silu in
+ * fp32 with IEEE division -- the bits torch's F.silu gives a bf16 CUDA tensor.  The epilogue reads these values from
+ * a table over the bf16 inputs (exact: the function depends on the 16 input bits only) and evaluates the formula for
+ * inputs outside it; this entry runs the same code, so one call over all 65536 bf16 patterns checks the epilogue's
+ * silu against torch's.  x and y bf16 (2-byte aligned; y may be x).
+ */
+int convrot_silu(const void* x, void* y, int64_t n, void* stream);
+
+/*
  * The Ulysses exchange fused into the kernels, over peer memory (no counterpart in the reference, whose all-to-all
  * is diffusers' NCCL call; call site distributed.py:88-96).  One process per GPU; every rank maps the others'
  * exchange buffers (convrot_ipc_*), so a chunk pointer below may name another GPU's memory.  At most 8 chunks.

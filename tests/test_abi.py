@@ -130,6 +130,11 @@ def test_fused_and_exchange_entry_points_reject_bad_arguments(lib):
     assert adaln(eps=float("nan")) == lib.ERR_ARG
     assert adaln(sc=None) == lib.ERR_ARG
     assert adaln(M=0) == lib.OK
+    # the epilogue's silu alone: a non-negative count, non-null 2-byte aligned pointers
+    assert L.convrot_silu(p, p, -1, None) == lib.ERR_SHAPE
+    assert L.convrot_silu(None, p, 8, None) == lib.ERR_ARG
+    assert L.convrot_silu(P(4097), p, 8, None) == lib.ERR_ALIGN
+    assert L.convrot_silu(None, None, 0, None) == lib.OK
     # scatter / gather: at least two and at most eight chunks, chunk widths the kernels can address
     outs = (P * 9)(*([4096] * 9))
     assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 256, 64, outs, 1, 128,

@@ -522,6 +522,45 @@ def test_fused_swiglu_is_bitwise_the_unfused_composition(M, K, N, r, bias, gemm_
     assert diff.max() <= 1 and (diff == 0).mean() >= 0.999
 
 
+def test_epilogue_silu_is_torch_silu_on_every_bf16_input():
+    """The SwiGLU epilogue's silu (its shared-memory table plus the formula for inputs outside it), run alone over
+    all 65536 bf16 bit patterns, gives torch's F.silu bit for bit (NaN where torch gives NaN)."""
+    from hyperflow_h3_flash_b200 import ffn
+
+    x = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).to(DEV)
+    y = ffn.silu_bf16(x)
+    ref = F.silu(x)
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(y), nan)
+    assert torch.equal(y.view(torch.int16)[~nan], ref.view(torch.int16)[~nan])
+    # every pattern checked bitwise but the 254 NaN inputs and -inf (silu(-inf) = -inf / inf = NaN)
+    assert int((~nan).sum()) == 65536 - 255
+
+
+def test_fused_swiglu_outside_the_silu_table_is_still_bitwise(gemm_mode):
+    """Projection outputs of magnitude zero, below 2^-19 or at least 32 are outside the epilogue's silu table and take
+    the formula; the fused result is still the unfused composition bit for bit."""
+    from hyperflow_h3_flash_b200 import ffn
+
+    K, N, M = 1024, 1024, 300
+    w = synthetic.linear_weights(K, N, rank=0, bias=False, group=256, seed_offset=9)
+    ws = w.wscale.clone()
+    ws[N // 2:N // 2 + 64] *= 1e-9  # g columns (the second half) with tiny magnitudes
+    ws[N // 2 + 64:N // 2 + 128] *= 200.0  # and with large ones
+    proj = I.Int8RotLinear(K, N, 256)
+    proj.qweight.copy_(w.qweight)
+    proj.wscale.copy_(ws)
+    proj = proj.to(DEV)
+    x = synthetic.activations(M, K, seed=73)
+    x[5] = 0  # a zero row: g = 0 in every column
+    x = x.to(DEV)
+    y = proj(x)
+    g = y[:, N // 2:].float()
+    assert (g[:, :64].abs() < 2.0 ** -19).float().mean() > 0.5 and (g[:, 64:128].abs() >= 32).any()
+    assert (g[5] == 0).all()
+    assert torch.equal(ffn.SwiGLUInt8(proj)(x), ffn.swiglu_reference(y))
+
+
 def test_fused_swiglu_gate_first_and_shape_checks():
     from hyperflow_h3_flash_b200 import ffn
 
