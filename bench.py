@@ -52,7 +52,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
-    ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "down"],
+    ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "rotate_ffn_down",
+                                       "down"],
                     default=None,
                     help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
     return ap.parse_args()
@@ -732,7 +733,10 @@ def run_case(args) -> None:
         mod_sc = (torch.randn(8, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
         mod_sh = (torch.randn(8, K_DIM, generator=gen) * 0.1).to(torch.bfloat16).to(dev)
         mod_idx = (torch.arange(M, device=dev) * 8 // M).to(torch.int32)
+    if args.case == "rotate_ffn_down":  # config 3's FFN-down input (K = 13824: the one-column kernel)
+        h = synthetic.activations(M, 13824, seed=2).to(dev)
     fns = {
+        "rotate_ffn_down": lambda: I.rotate_quant(h, GROUP),
         "rotate_adaln": lambda: I.rotate_quant_adaln(x, GROUP, mod_sc, mod_sh, mod_idx),
         "gemm_ffn_up": lambda: I.convrot_matmul(q, wf.qweight, s, wf.wscale, bias=wf.bias, xa=xa64, up=wf.up,
                                                 swiglu=True),
