@@ -631,7 +631,8 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     def adaln_fused():
         return I.rotate_quant_adaln(xb, GROUP, mod_scale, mod_shift, mod_idx)
 
-    out["adaln_prologue_cfg3"] = {"config": "M=32760, K=5120, 8 modulation rows: LayerNorm + modulate + rotate+quantise",
+    out["adaln_prologue_cfg3"] = {"config": "M=32760, K=5120, 8 modulation rows: LayerNorm + modulate + "
+                                            "rotate+quantise",
                                   **{f"ms_{k}": v for k, v in timed_ab({"unfused": adaln_unfused,
                                                                         "fused": adaln_fused}, args.steps).items()}}
 
@@ -672,15 +673,37 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     def kv(t):
         return kv_layers[0](t), kv_layers[1](t)
 
+    from hyperflow_h3_flash_b200.grouped import GroupedInt8RotLinear
+
+    kv_group = GroupedInt8RotLinear(*kv_layers)
     cfg5 = {}
     for rows in (256, 333):
         xt = synthetic.activations(rows, 4096, seed=rows).to(dev)
         graphed = CapturedCall(kv, xt)
-        t = timed_ab({"eager": lambda: kv(xt), "graph": lambda: graphed(xt)}, args.steps * 5)
-        cfg5[f"M{rows}"] = {"eager_us": t["eager"] * 1e3, "graph_us": t["graph"] * 1e3}
+        graphed_group = CapturedCall(kv_group, xt)
+        t = timed_ab({"eager": lambda: kv(xt), "graph": lambda: graphed(xt),
+                      "grouped_graph": lambda: graphed_group(xt)}, args.steps * 5)
+        cfg5[f"M{rows}"] = {"eager_us": t["eager"] * 1e3, "graph_us": t["graph"] * 1e3,
+                            "grouped_graph_us": t["grouped_graph"] * 1e3}
     out["cross_attention_kv_cfg5"] = {"config": "config 5: K and V projections 4096 -> 5120 (r=32, bias, shared "
-                                                "quantisation) on 256 / 333 text tokens, per call",
+                                                "quantisation) on 256 / 333 text tokens, per call; grouped = one "
+                                                "quantisation, one down projection and one GEMM launch for both",
                                       **cfg5}
+
+    # config 2's q / k / v as three layers (shared quantisation and down projection) or as one grouped launch
+    qkv_layers = []
+    for i in range(3):
+        wl = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=60 + i)
+        ly = I.Int8RotLinear(K_DIM, N_DIM, GROUP, bias=True, rank=RANK)
+        synthetic.load_into(ly, wl)
+        qkv_layers.append(ly.to(dev))
+    I.share_lowrank(*qkv_layers)
+    qkv_layers[0].keep_input = qkv_layers[1].keep_input = True
+    qkv_group = GroupedInt8RotLinear(*qkv_layers)
+    t = timed_ab({"separate": lambda: [ly(x) for ly in qkv_layers], "grouped": lambda: qkv_group(x)}, args.steps)
+    out["qkv_cfg2"] = {"config": f"config 2's q, k, v (M={M}, K=N={K_DIM}, r={RANK}, bias): three layers sharing "
+                                 "quantisation and down projection, or one grouped GEMM launch",
+                       "separate_ms": t["separate"], "grouped_ms": t["grouped"]}
 
     t = timed_ab({"unfused": block_unfused, "fused": block_fused}, steps_b)
     ms_bu, ms_bf = t["unfused"], t["fused"]

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
                                _P], _I),
     "convrot_gemm_swiglu": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _L, _P], _I),
     "convrot_silu": ([_P, _P, _L, _P], _I),
+    "convrot_gemm_grouped": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _L, _P], _I),
     "convrot_gemm_scatter": ([_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _P, _I, _L, _P], _I),
     "convrot_rotate_quant_gather": ([_P, _I, _L, _L, _L, _I, _I, _P, _L, _P, _P, _L, _P], _I),
     "convrot_ipc_handle": ([_P, _P, _P], _I),

@@ -255,8 +255,9 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
             const void* bias, const void* xa, int64_t ldxa, const void* up, int64_t ld_up, int64_t r, int64_t M,
             int64_t N, int64_t K, void* out, int64_t ldo, bool raw, cudaStream_t stream,
             void* const* chunks = nullptr, int n_chunks = 1, bool swiglu = false,
-            const ResidualArgs* residual = nullptr) {
+            const ResidualArgs* residual = nullptr, int lr_segments = 1) {
   if (n_chunks < 1 || n_chunks > kMaxChunks || (n_chunks > 1 && !chunks)) return CONVROT_ERR_ARG;
+  if (lr_segments < 1 || lr_segments > kMaxChunks) return CONVROT_ERR_ARG;
   if (swiglu && (raw || n_chunks > 1)) return CONVROT_ERR_ARG;
   if (residual) {
     if (raw || swiglu || n_chunks > 1 || !residual->res) return CONVROT_ERR_ARG;
@@ -287,8 +288,12 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   if (ldq % 16 || ldw % 16 || !aligned16(q) || !aligned16(w)) return CONVROT_ERR_ALIGN;
   if (raw ? (ldo % 4 || !aligned16(out)) : (ldo % 8 || !aligned16(out))) return CONVROT_ERR_ALIGN;
   if (!raw && (!aligned16(ws) || (bias && !aligned16(bias)))) return CONVROT_ERR_ALIGN;
-  if (has_lr && (ldxa < r || ld_up < r || ldxa % 8 || ld_up % 8 || !aligned16(xa) || !aligned16(up)))
-    return ldxa < r || ld_up < r ? CONVROT_ERR_SHAPE : CONVROT_ERR_ALIGN;
+  if (has_lr && (ldxa < r * lr_segments || ld_up < r || ldxa % 8 || ld_up % 8 || !aligned16(xa) || !aligned16(up)))
+    return ldxa < r * lr_segments || ld_up < r ? CONVROT_ERR_SHAPE : CONVROT_ERR_ALIGN;
+  // Segments (layers stacked along N): whole 256-column tiles per segment, and each segment's xa columns start on a
+  // 16-byte boundary (the TMA load's inner coordinate).
+  if (lr_segments > 1 && (!has_lr || N % lr_segments || (N / lr_segments) % 256 || r % 8 || swiglu || residual))
+    return has_lr && !swiglu && !residual ? CONVROT_ERR_SHAPE : CONVROT_ERR_ARG;
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
@@ -308,7 +313,8 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   if ((rc = make_map(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K, ldw, b_rows, 128))) return rc;
   const int lr_atom = r <= 32 ? 64 : 128;
   if (has_lr) {
-    if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r, ldxa, kBM, lr_atom / 2))) return rc;
+    if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r * lr_segments, ldxa, kBM, lr_atom / 2)))
+      return rc;
     if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, b_rows, lr_atom / 2))) return rc;
   }
   GemmParams p;
@@ -333,6 +339,7 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   }
   p.a_chunk = static_cast<int>(K);
   p.r = has_lr ? static_cast<int>(r) : 0;
+  p.lr_seg_n = lr_segments > 1 ? static_cast<int>(N / lr_segments) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   if (two_sm) {
@@ -731,6 +738,18 @@ int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
                         int64_t M, int64_t N, int64_t K, void* h, int64_t ldh, void* stream) {
   return gemm_i8(q, ldq, w, ldw, sx, ws, bias, xa, ldxa, lr_up, ld_up, r, M, N, K, h, ldh, false,
                  static_cast<cudaStream_t>(stream), nullptr, 1, true);
+}
+
+int convrot_gemm_grouped(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                         const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                         int64_t M, int64_t N, int64_t K, int segments, void* const* y_chunks, int64_t ldy,
+                         void* stream) {
+  if (segments < 2 || segments > kMaxChunks || !y_chunks) return CONVROT_ERR_ARG;
+  if (r > 0 && (!xa || !lr_up)) return CONVROT_ERR_ARG;
+  // without a low-rank term the segments need no xa offsets: the chunked output alone separates the layers
+  return gemm_i8(q, ldq, w, ldw, sx, ws, bias, r > 0 ? xa : nullptr, ldxa, r > 0 ? lr_up : nullptr, ld_up, r, M, N, K,
+                 nullptr, ldy, false, static_cast<cudaStream_t>(stream), y_chunks, segments, false, nullptr,
+                 r > 0 ? segments : 1);
 }
 
 int convrot_silu(const void* x, void* y, int64_t n, void* stream) {

@@ -56,6 +56,7 @@ struct GemmParams {
   const int32_t* gate_index;
   int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
+  int lr_seg_n;         // > 0: output columns [s lr_seg_n, (s + 1) lr_seg_n) read xa columns [s r, (s + 1) r)
   uint64_t wait_limit_ns;
   int* error_word;
 };
@@ -569,9 +570,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
+          const int xs = p.lr_seg_n ? (n0 / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
           for (int a = 0; a < LR_ATOMS; ++a) {
             const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
-            tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, x, m0);
+            tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, x + xs, m0);
             tma_load_2d(lr_up + a * BN * LR_ATOM, &tmap_up, lr_full, x, n0);
           }
           loaded = true;

@@ -422,9 +422,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             break;
           }
           if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
+          const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
           for (int a = 0; a < LR_ATOMS; ++a) {
             const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
-            tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x, m0);
+            tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x + xs, m0);
             tma_load_2d_pair(lr_up + a * Cfg::kBHalf * LR_ATOM, &tmap_up, leader_lr_full, x, n0);
           }
         }

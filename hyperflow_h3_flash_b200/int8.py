@@ -267,7 +267,8 @@ class Int8RotLinear(nn.Module):
 def _stacked_down(peers: tuple) -> Tensor:
     """``[down_q; down_k; down_v]`` for layers joined by ``share_lowrank``, built once and rebuilt only when one of
     the weights is replaced, moved or modified in place (kept on the first layer, keyed by address and version)."""
-    key = tuple((layer.down.weight.data_ptr(), layer.down.weight._version) for layer in peers)
+    weights = [layer.down.weight for layer in peers]
+    key = tuple((w.data_ptr(), None if w.is_inference() else w._version) for w in weights)  # no version: inference
     cached = getattr(peers[0], "_stacked_down_cache", None)
     if cached is None or cached[0] != key:
         with torch.no_grad():
@@ -465,7 +466,7 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
                    xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None,
                    out_ptrs: list[int] | None = None, out_ld: int | None = None,
                    swiglu: bool = False, residual: Tensor | None = None, gate: Tensor | None = None,
-                   gate_index: Tensor | None = None) -> Tensor | None:
+                   gate_index: Tensor | None = None, segments: int | None = None) -> Tensor | list[Tensor] | None:
     """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
 
     ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout).  ``out_ptrs`` (device
@@ -473,7 +474,11 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
     returns None: the Ulysses exchange done by the GEMM's stores.  ``swiglu`` treats b (and sb, bias, up) as a gated
     projection interleaved in 32-row blocks (``ffn.interleave_rows``) and returns ``h = a * silu(g)``, ``[M, N / 2]``.
     ``residual`` (bf16 ``[M, N]``) returns ``residual + gate[gate_index] * y`` in bf16 steps (``gate`` bf16
-    ``[T, N]`` or ``[N]``, optional; ``gate_index`` ``[M]``, optional: row 0 for every token)."""
+    ``[T, N]`` or ``[N]``, optional; ``gate_index`` ``[M]``, optional: row 0 for every token).
+
+    ``segments = S`` treats b (and sb, bias, up) as S layers stacked along N that read the same input, and returns
+    their S outputs ``[M, N / S]`` from one launch; ``xa`` is then ``[M, S * r]`` (layer s's down projection in columns
+    ``[s r, (s + 1) r)``) and ``up`` ``[N, r]``."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -491,6 +496,8 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
         bias = bias.reshape(-1).to(torch.bfloat16).contiguous()
         if bias.numel() != N:
             raise ValueError("bias size does not match N")
+    if segments:
+        return _grouped_matmul(a_s, b_s, sa, sb, bias, xa, up, segments, M, N, Kp)
     r = 0
     if xa is not None or up is not None:
         if xa is None or up is None:
@@ -570,6 +577,34 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
                                  up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(y), ldy, _stream(a))
     _lib.check(rc, "convrot_gemm")
     return y if ldy == N else y[:, :N]
+
+
+def _grouped_matmul(a_s: Tensor, b_s: Tensor, sa: Tensor, sb: Tensor, bias: Tensor | None, xa: Tensor | None,
+                    up: Tensor | None, S: int, M: int, N: int, Kp: int) -> list[Tensor]:
+    """``convrot_gemm_grouped``: S stacked layers, one launch, S outputs (see ``convrot_matmul(segments=S)``)."""
+    if S < 2 or N % S:
+        raise ValueError(f"N = {N} does not split into {S} layers")
+    Ns = N // S
+    r = 0
+    if xa is not None or up is not None:
+        if xa is None or up is None:
+            raise ValueError("the low-rank term needs both xa and up")
+        r = up.shape[1]
+        if up.shape[0] != N or xa.shape[1] != S * r:
+            raise ValueError(f"grouped low-rank operands: xa {tuple(xa.shape)}, up {tuple(up.shape)} for {S} layers")
+        if r % 8 or Ns % 256 or r > MAX_FUSED_RANK:
+            raise ValueError(f"a grouped low-rank term needs r % 8 == 0 (r = {r}) and N / S % 256 == 0 (N / S = {Ns})")
+        xa = _pad_cols(xa.to(torch.bfloat16), S * r)
+        up = _pad_cols(up.to(torch.bfloat16).contiguous(), r)
+    elif Ns % 32:
+        raise ValueError(f"grouped outputs need N / S % 32 == 0, got N / S = {Ns}")
+    outs = [torch.empty(M, Ns, dtype=torch.bfloat16, device=a_s.device) for _ in range(S)]
+    ptrs = (ctypes.c_void_p * S)(*[o.data_ptr() for o in outs])
+    rc = _lib.lib().convrot_gemm_grouped(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                         _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                         up.stride(0) if up is not None else 0, r, M, N, Kp, S, ptrs, Ns, _stream(a_s))
+    _lib.check(rc, "convrot_gemm_grouped")
+    return outs
 
 
 def int8_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor) -> Tensor:

@@ -158,6 +158,20 @@ int convrot_gemm_swiglu(const int8_t* q, int64_t ldq, const int8_t* w, int64_t l
                         int64_t M, int64_t N, int64_t K, void* h, int64_t ldh, void* stream);
 
 /*
+ * Several linears that read one input (to_q / to_k / to_v, or a cross-attention's to_k / to_v), as ONE GEMM launch
+ * (no counterpart in the reference: one convrot_gemm per layer).  Their weights are stacked along N: w, ws, bias and
+ * lr_up hold `segments` layers of N / segments output columns each, and layer s writes y_chunks[s] ([M, N / segments],
+ * leading dimension ldy).  Every layer has the same rank r (or none): xa is [M, segments * r] with layer s's down
+ * projection in columns [s r, (s + 1) r) (what one down projection over the stacked down weights produces), and
+ * lr_up's rows of layer s are its up weights.  With r > 0, N / segments must be a multiple of 256 (whole tiles per
+ * layer) and r a multiple of 8; 2 <= segments <= 8.  Results are bitwise those of the separate convrot_gemm calls.
+ */
+int convrot_gemm_grouped(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
+                         const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
+                         int64_t M, int64_t N, int64_t K, int segments, void* const* y_chunks, int64_t ldy,
+                         void* stream);
+
+/*
  * The SwiGLU epilogue's silu alone, elementwise: y[i] = bf16( x[i] / (1 + exp(-x[i])) ) over n bf16 values, silu in
  * fp32 with IEEE division -- the bits torch's F.silu gives a bf16 CUDA tensor.  The epilogue reads these values from
  * a table over the bf16 inputs (exact: the function depends on the 16 input bits only) and evaluates the formula for

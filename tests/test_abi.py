@@ -137,6 +137,15 @@ def test_fused_and_exchange_entry_points_reject_bad_arguments(lib):
     assert L.convrot_silu(None, None, 0, None) == lib.OK
     # scatter / gather: at least two and at most eight chunks, chunk widths the kernels can address
     outs = (P * 9)(*([4096] * 9))
+    # grouped layers: 2 to 8 segments, whole 256-column tiles per low-rank segment, ranks a multiple of 8
+    def grouped(r, N, S, xa=p):
+        return L.convrot_gemm_grouped(p, 64, p, 64, p, p, None, xa, 64, p, 64, r, 4, N, 64, S, outs, 256, None)
+
+    assert grouped(32, 512, 1) == lib.ERR_ARG
+    assert grouped(32, 512 * 9, 9) == lib.ERR_ARG
+    assert grouped(32, 384, 2) == lib.ERR_SHAPE  # 192-column segments with a low-rank term
+    assert grouped(12, 512, 2) == lib.ERR_SHAPE  # rank 12
+    assert grouped(32, 512, 2, xa=None) == lib.ERR_ARG
     assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 256, 64, outs, 1, 128,
                                   None) == lib.ERR_ARG
     assert L.convrot_gemm_scatter(p, 64, p, 64, p, p, None, None, 0, None, 0, 0, 4, 288, 64, outs, 9, 32,

@@ -758,3 +758,46 @@ def test_captured_graph_replays_the_layer_bitwise(M, K, N):
         k_g, v_g = graphed(x)
         k_e, v_e = kv(x)
         assert torch.equal(k_g, k_e) and torch.equal(v_g, v_e)
+
+
+@pytest.mark.parametrize("M,K,N,S,r,bias", [(40, 1024, 512, 3, 32, True), (333, 1024, 512, 2, 32, True),
+                                             (4096, 1024, 512, 3, 0, False), (8, 1024, 512, 2, 64, True),
+                                             (777, 1024, 768, 2, 48, True), (256, 4096, 5120, 2, 32, True)])
+def test_grouped_layers_are_bitwise_the_separate_layers(M, K, N, S, r, bias, gemm_mode):
+    """GroupedInt8RotLinear (one quantisation, one down projection, one GEMM launch writing each layer's output)
+    gives each layer's own forward bit for bit, on the 1-SM and the 2-SM kernel; r = 48 makes a layer's rank chunk
+    run past its xa columns into the next layer's, where its zero-filled up columns must cancel them exactly."""
+    from hyperflow_h3_flash_b200.grouped import GroupedInt8RotLinear
+
+    layers = []
+    for s in range(S):
+        w = synthetic.linear_weights(K, N, rank=r, bias=bias, group=256, seed_offset=90 + s)
+        ly = I.Int8RotLinear(K, N, 256, bias=bias, rank=r)
+        synthetic.load_into(ly, w)
+        layers.append(ly.to(DEV))
+    group = GroupedInt8RotLinear(*layers)
+    x = synthetic.activations(M, K, seed=91).to(DEV)
+    outs = group(x)
+    assert len(outs) == S
+    for ly, o in zip(layers, outs, strict=True):
+        assert o.shape == (M, N)
+        assert torch.equal(o, ly(x))
+
+
+def test_grouped_layers_follow_weight_updates():
+    from hyperflow_h3_flash_b200.grouped import GroupedInt8RotLinear
+
+    layers = []
+    for s in range(2):
+        w = synthetic.linear_weights(512, 256, rank=16, bias=True, group=256, seed_offset=95 + s)
+        ly = I.Int8RotLinear(512, 256, 256, bias=True, rank=16)
+        synthetic.load_into(ly, w)
+        layers.append(ly.to(DEV))
+    group = GroupedInt8RotLinear(*layers)
+    x = synthetic.activations(300, 512, seed=96).to(DEV)
+    group(x)
+    with torch.no_grad():
+        layers[1].wscale.mul_(2.0)
+        layers[0].up.weight.mul_(-1.0)
+    outs = group(x)
+    assert torch.equal(outs[0], layers[0](x)) and torch.equal(outs[1], layers[1](x))
