@@ -298,8 +298,18 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   int rc = device_state(&st);
   if (rc) return rc;
 
-  // The 2-SM kernel (256 x 256 per CTA pair) unless the rows fit one 128-row tile or a mode is forced.
-  const bool two_sm = g_gemm_mode == 2 || (g_gemm_mode == 0 && M > kBM);
+  // Both kernels do the same work per SM and tile (128 rows x 256 columns) and give identical bits.  Automatic mode
+  // takes the one with fewer waves of tiles, and the 1-SM kernel whenever its tiles fit one wave (it skips the
+  // pair's cluster start-up: 31-32 against 33-49 us on B200 for single-wave shapes at M = 200-500); otherwise the
+  // 2-SM kernel, whose halved B traffic per SM makes each tile cheaper at full load.
+  bool two_sm = g_gemm_mode == 2;
+  if (g_gemm_mode == 0 && M > kBM) {
+    const int64_t n_tiles = (N + 255) / 256;
+    const int64_t sms = st->sms > 1 ? st->sms : 2;
+    const int64_t waves1 = ((M + kBM - 1) / kBM * n_tiles + sms - 1) / sms;
+    const int64_t waves2 = ((M + 2 * kBM - 1) / (2 * kBM) * n_tiles + sms / 2 - 1) / (sms / 2);
+    two_sm = !(waves1 <= 1 || waves1 < waves2);
+  }
   const int b_rows = two_sm ? 128 : 256;  // B rows per CTA tile
   CUtensorMap ta, tb, txa, tup;
   memset(&txa, 0, sizeof(txa));

@@ -275,7 +275,8 @@ void convrot_set_wait_limit_ns(uint64_t ns);
 
 /*
  * Which INT8 GEMM kernel convrot_gemm / convrot_gemm_acc / convrot_linear launch: 0 = automatic (the 2-SM
- * cta_group::2 kernel with 256 x 256 tiles per CTA pair when M > 128, else the 1-SM 128 x 256 kernel),
+ * cta_group::2 kernel with 256 x 256 tiles per CTA pair, unless the 1-SM 128 x 256 kernel's tiles fit one wave on
+ * the GPU's SMs or need fewer waves than the pairs' tiles; M <= 128 always takes the 1-SM kernel),
  * 1 = always the 1-SM kernel, 2 = always the 2-SM kernel.  Both give bitwise identical results.
  * Process-wide; returns CONVROT_ERR_ARG for other values.
  */
