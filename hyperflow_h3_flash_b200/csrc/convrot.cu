@@ -197,8 +197,29 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
   // HBM-bound with few tiles: two per SM keeps every tile of a 32k-row input in flight at once).
   const int per_sm = (Cfg::kSmemBytes <= 113 * 1024 && Cfg::kTmemCols <= 256) ? 2 : 1;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
+  if (p.split_k > 1) {  // clusters of split_k CTAs, one tile per cluster (EPI_BF16 split K)
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * p.split_k), 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    memset(&attr, 0, sizeof(attr));
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(p.split_k);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, txa, tup, p);
+    if (e == cudaSuccess) return CONVROT_OK;
+    cudaGetLastError();  // a cluster the GPU cannot place: run the unsplit kernel below
+  }
+  GemmParams q = p;
+  q.split_k = 1;
   const int grid = tiles < per_sm * st.sms ? tiles : per_sm * st.sms;
-  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, p);
+  kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, txa, tup, q);
   e = cudaGetLastError();
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
@@ -407,6 +428,15 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
   p.a_chunk = static_cast<int>(x_chunk);
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
+  // Few row tiles (M <= 1024): split K over a cluster of up to 8 CTAs per tile, so the serial K loop of each tile is
+  // shared instead of running on one SM.  The split depends on M and K only, so layers that share an input compute
+  // each xa column with the same additions whether their down projections run stacked or one by one.
+  const int64_t nkb = (K + 63) / 64;
+  if (M <= 8 * kBM && nkb >= 4) {
+    int split = 1;
+    while (split * 2 <= 8 && split * 2 <= nkb / 2) split *= 2;
+    p.split_k = split;
+  }
   switch (bn) {
     case 32: return launch_gemm<CfgDown<32, 5>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);
     case 64: return launch_gemm<CfgDown<64, 4>, KIND_BF16, EPI_BF16, 0, 0>(*st, ta, tb, tz, tz, p, stream);

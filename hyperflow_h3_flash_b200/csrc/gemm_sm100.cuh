@@ -57,6 +57,7 @@ struct GemmParams {
   int a_chunk;          // W of operand A along K (K for plain rows); its TMA map is 3-D (W, M, K / W)
   int r;                // low-rank width (0 = none)
   int lr_seg_n;         // > 0: output columns [s lr_seg_n, (s + 1) lr_seg_n) read xa columns [s r, (s + 1) r)
+  int split_k;          // > 1 (the bf16 down projection only): clusters of split_k CTAs split K, one tile each
   uint64_t wait_limit_ns;
   int* error_word;
 };
@@ -349,6 +350,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const int lr_chunks = HAS_LR ? (p.r + LR_ATOMS * (LR_ATOM / 2) - 1) / (LR_ATOMS * (LR_ATOM / 2)) : 0;
   const int nkb = (p.K * (KIND == KIND_I8 ? 1 : 2) + kRowBytes - 1) / kRowBytes;
   constexpr int kKPerStage = KIND == KIND_I8 ? 128 : 64;  // elements
+  // Split K (EPI_BF16, few row tiles): the launch is clusters of ksplit CTAs with one tile per cluster; CTA s of a
+  // cluster accumulates the K stages [s nkb / ksplit, (s + 1) nkb / ksplit), and the cluster sums the partial tiles
+  // through distributed shared memory at the end of the kernel, in the order s = 0, 1, ... for every element.
+  const int ksplit = EPI == EPI_BF16 && p.split_k > 1 ? p.split_k : 1;
+  const int krank = ksplit > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int kb_begin = krank * nkb / ksplit, kb_end = (krank + 1) * nkb / ksplit;
+  const int tile0 = static_cast<int>(blockIdx.x) / ksplit, tile_step = static_cast<int>(gridDim.x) / ksplit;
+  constexpr int kPartStride = BN + 4;  // floats per row of a partial tile (16-byte pad: conflict-free rows)
+  static_assert(KIND != KIND_BF16 || kBM * kPartStride * 4 <= S * Cfg::kStageBytes, "partial tile beyond the ring");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -395,12 +405,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t stage = 0, phase = 0;
       uint32_t issued_mask = 0, issued_parity = 0;  // last load per stage, for draining after an abort
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tile_step) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * kBM;
         const int n0 = nb * BN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, limit, abort_flag)) {
             fail();
             ok = false;
@@ -487,7 +497,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         return true;
       };
       int i = 0;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++i) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tile_step, ++i) {
         const uint32_t buf = i & 1;
         if (!mbar_wait_bounded(&tmem_empty[buf], ((i >> 1) & 1) ^ 1, limit, abort_flag)) {
           ok = false;
@@ -495,7 +505,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           // wait for the stage, issuing a pending low-rank MMA while the data is in flight
           if (HAS_LR) {
             const uint64_t t0 = globaltimer_ns();
@@ -520,9 +530,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           for (int kk = 0; kk < Cfg::kMmaPerStage; ++kk) {
             // +32 bytes of K inside the 128-byte swizzle atom: +2 in the (addr >> 4) field
             if (KIND == KIND_I8)
-              mma_i8(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
+              mma_i8(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, kb != kb_begin || kk != 0);
             else
-              mma_f16(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
+              mma_f16(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, kb != kb_begin || kk != 0);
           }
           mma_commit(&empty[stage]);
           if (++stage == S) {
@@ -557,7 +567,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t loaded_parity = 0;
       int u = 0;  // rank chunks loaded so far (all tiles)
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = tile0; ok && tile < num_tiles; tile += tile_step) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * kBM;
@@ -590,7 +600,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
     int i = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+    for (int tile = tile0; tile < num_tiles; tile += tile_step, ++i) {
       const uint32_t buf = i & 1;
       const uint32_t par = (i >> 1) & 1;
       int mb, nb;
@@ -685,6 +695,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           tmem_ld_32x32b_x32(taddr + c, v);
           tmem_ld_wait();
           const int n = n0 + c;
+          if (ksplit > 1) {  // this CTA's partial row, into the operand ring (idle: the tile's loads are consumed)
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(ring) + row_in_tile * kPartStride + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                   __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            continue;
+          }
           if (!row_ok) continue;
           float t[32];
 #pragma unroll
@@ -700,6 +718,40 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (ksplit > 1) {
+    // Every CTA of the cluster reaches both barriers (the roles above return only through here).  Between them,
+    // the epilogue warps of CTA s sum columns [s BN / ksplit, (s + 1) BN / ksplit) of the tile over the cluster's
+    // partials, in rank order, and store them as bf16.
+    cluster_sync();
+    if (warp >= 2 && warp <= 5 && tile0 < num_tiles) {
+      int mb, nb;
+      tile_coords(tile0, num_m, num_n, mb, nb);
+      const int row_in_tile = (warp & 3) * 32 + lane;
+      const int row = mb * kBM + row_in_tile;
+      const int cols = BN / ksplit;  // a multiple of 4
+      const int c0 = krank * cols;
+      const uint32_t mine = smem_u32(reinterpret_cast<float*>(ring) + row_in_tile * kPartStride);
+      if (row < p.M) {
+        __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<int64_t>(row) * p.ldo;
+        for (int c = c0; c < c0 + cols; c += 4) {
+          const int n = nb * BN + c;
+          if (n >= p.N) break;
+          float4 acc = ld_shared_cluster_v4(mapa_shared(mine + c * 4, 0));
+          for (int r = 1; r < ksplit; ++r) {
+            const float4 t = ld_shared_cluster_v4(mapa_shared(mine + c * 4, r));
+            acc.x = __fadd_rn(acc.x, t.x);
+            acc.y = __fadd_rn(acc.y, t.y);
+            acc.z = __fadd_rn(acc.z, t.z);
+            acc.w = __fadd_rn(acc.w, t.w);
+          }
+          const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+          *reinterpret_cast<uint2*>(orow + n) =
+              make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        }
+      }
+    }
+    cluster_sync();  // the partials stay in place until every CTA of the cluster has read them
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<Cfg::kTmemCols>(tmem_base);

@@ -153,7 +153,9 @@ def test_gemm_and_rescale_are_bitwise_the_reference_kernels(gemm_mode):
 # ---------------------------------------------------------------------------------------------- low-rank + bias
 
 
-@pytest.mark.parametrize("M,K,r", [(40, 1024, 16), (333, 4096, 32), (256, 5120, 64), (17, 520, 48)])
+# M <= 1024 splits K over a cluster of CTAs (2-8 by K); 1025 rows and up run unsplit
+@pytest.mark.parametrize("M,K,r", [(40, 1024, 16), (333, 4096, 32), (256, 5120, 64), (17, 520, 48),
+                                   (1024, 4096, 256), (1025, 1024, 96), (17, 256, 16), (5, 8192, 128)])
 def test_lowrank_down_within_one_bf16_ulp(M, K, r):
     x = synthetic.activations(M, K, seed=7)
     g = torch.Generator().manual_seed(9)
