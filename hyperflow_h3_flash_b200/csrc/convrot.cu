@@ -154,7 +154,12 @@ void store_resident(const void* fn, int resident) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_launch_cache_n < kLaunchCacheSize) g_launch_cache[g_launch_cache_n++] = {fn, dev, resident};
+  if (g_launch_cache_n < kLaunchCacheSize) {
+    LaunchCache& c = g_launch_cache[g_launch_cache_n++];
+    c.fn = fn;
+    c.dev = dev;
+    c.resident = resident;
+  }
 }
 
 // 3-D map over "chunked rows": element (m, k) at base + (k / W) * S + m * L + k % W, i.e. dims (W, M, K / W) with
@@ -198,14 +203,12 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
   const int per_sm = (Cfg::kSmemBytes <= 113 * 1024 && Cfg::kTmemCols <= 256) ? 2 : 1;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
   if (p.split_k > 1) {  // clusters of split_k CTAs, one tile per cluster (EPI_BF16 split K)
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(tiles * p.split_k), 1, 1);
     cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr;
-    memset(&attr, 0, sizeof(attr));
+    cudaLaunchAttribute attr = {};
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = static_cast<unsigned>(p.split_k);
     attr.val.clusterDim.y = 1;
@@ -236,8 +239,7 @@ int launch_gemm2(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap
   if (clusters < 0) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e);
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof(cfg));
+    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * st.sms, 1, 1);
     cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
