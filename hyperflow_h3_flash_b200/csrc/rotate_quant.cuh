@@ -367,7 +367,14 @@ __device__ __forceinline__ uint32_t adaln_pair(uint32_t w, uint32_t sc, uint32_t
   const uint32_t n = bf16x2_rn(__fmul_rn(__fsub_rn(bf16_lo(w), mean), rstd),
                                __fmul_rn(__fsub_rn(bf16_hi(w), mean), rstd));
   const uint32_t one_s = bf16x2_rn(__fadd_rn(1.0f, bf16_lo(sc)), __fadd_rn(1.0f, bf16_hi(sc)));
-  const uint32_t t = bf16x2_rn(__fmul_rn(bf16_lo(n), bf16_lo(one_s)), __fmul_rn(bf16_hi(n), bf16_hi(one_s)));
+  // bf16 * bf16 is exact in fp32 (16 significant bits, same exponent range), so rounding the fp32 product to bf16
+  // is one rounding of the exact product: what the packed bf16 multiply computes, in one instruction for the pair.
+  __nv_bfloat162 nb, ob;
+  memcpy(&nb, &n, 4);
+  memcpy(&ob, &one_s, 4);
+  const __nv_bfloat162 tb = __hmul2(nb, ob);
+  uint32_t t;
+  memcpy(&t, &tb, 4);
   return bf16x2_rn(__fadd_rn(bf16_lo(t), bf16_lo(sh)), __fadd_rn(bf16_hi(t), bf16_hi(sh)));
 }
 
