@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import numpy as np
+import pytest
 import torch
 import torch.nn.functional as F
 
@@ -68,3 +69,10 @@ def test_oracle_adaln_matches_torch_layer_norm_composition_within_one_ulp():
     # t + shift can cancel: bound by one bf16 ulp of the final add's operands
     t = (n * (1.0 + scale.index_select(0, idx))).float().abs() + shift.index_select(0, idx).float().abs()
     assert (np.abs(O.bf16_to_f32(got) - ref.float().numpy()) <= t.numpy() * 2.0**-5).all()
+
+
+def test_epilogue_silu_takes_bf16_cuda_tensors_only():
+    with pytest.raises(ValueError, match="bf16 CUDA"):
+        ffn.silu_bf16(torch.zeros(4, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="bf16 CUDA"):
+        ffn.silu_bf16(torch.zeros(4))
