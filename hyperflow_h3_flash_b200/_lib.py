@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_set_rotate_variant": ([_I], _I),
     "convrot_set_rotate_tuning": ([_I, _I], _I),
     "convrot_version": ([], _I),
+    "convrot_split_k_fallbacks": ([], _L),
 }
 
 

@@ -10,6 +10,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/convrot.h"
@@ -35,6 +36,7 @@ uint64_t g_wait_limit_ns = 2000000000ull;
 int g_gemm_mode = 0;  // 0 auto, 1 one-SM kernel, 2 two-SM kernel
 int g_rq_variant = 0;  // G = 256 rotation: 0 two-column team kernel, 1 one-column kernel
 int g_rq_stages = 0, g_rq_blocks = 0;  // rotation tuning overrides (0 = automatic)
+std::atomic<int64_t> g_split_fallbacks{0};  // split-K down projections that ran unsplit (cluster not placeable)
 
 struct DeviceState {
   bool ready = false;
@@ -202,22 +204,37 @@ int launch_gemm(const DeviceState& st, const CUtensorMap& ta, const CUtensorMap&
   // HBM-bound with few tiles: two per SM keeps every tile of a 32k-row input in flight at once).
   const int per_sm = (Cfg::kSmemBytes <= 113 * 1024 && Cfg::kTmemCols <= 256) ? 2 : 1;
   const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + Cfg::kBN - 1) / Cfg::kBN);
-  if (p.split_k > 1) {  // clusters of split_k CTAs, one tile per cluster (EPI_BF16 split K)
-    cudaLaunchConfig_t cfg = {};
+  bool split = p.split_k > 1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr = {};
+  if (split) {  // clusters of split_k CTAs, one tile per cluster (EPI_BF16 split K)
     cfg.gridDim = dim3(static_cast<unsigned>(tiles * p.split_k), 1, 1);
     cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr = {};
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = static_cast<unsigned>(p.split_k);
     attr.val.clusterDim.y = 1;
     attr.val.clusterDim.z = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, txa, tup, p);
-    if (e == cudaSuccess) return CONVROT_OK;
-    cudaGetLastError();  // a cluster the GPU cannot place: run the unsplit kernel below
+    // Whether the GPU can place one such cluster at all, asked once per (kernel, split) and cached under a key of
+    // its own (the kernel's address offset by the split, which no other entry uses).
+    const void* key = reinterpret_cast<const char*>(kernel) + p.split_k;
+    int placeable = -1;
+    if ((rc = cached_resident(key, &placeable))) return rc;
+    if (placeable < 0) {
+      int clusters = 0;
+      if ((e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg)) != cudaSuccess) return cuda_fail(e);
+      placeable = clusters > 0 ? 1 : 0;
+      store_resident(key, placeable);
+    }
+    if (placeable) {
+      e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, txa, tup, p);
+      return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
+    }
+    // The unsplit kernel below instead (counted: its K order, and so possibly the last bit of xa, differs).
+    g_split_fallbacks.fetch_add(1, std::memory_order_relaxed);
   }
   GemmParams q = p;
   q.split_k = 1;
@@ -903,8 +920,8 @@ int convrot_gemm_acc(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
 
 size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r) {
   if (M < 0 || K < 0 || r < 0) return 0;
-  return align256(static_cast<size_t>(M) * K) + align256(static_cast<size_t>(M) * 4) +
-         align256(static_cast<size_t>(M) * r * 2);
+  // exactly what convrot_linear checks: q rows padded to 16 bytes, xa rows to 8 elements (16 bytes)
+  return linear_workspace_need(M, K, r);
 }
 
 int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, const float* ws, const void* bias,
@@ -1005,5 +1022,7 @@ int convrot_set_gemm_mode(int mode) {
 }
 
 int convrot_version(void) { return 100; }
+
+int64_t convrot_split_k_fallbacks(void) { return g_split_fallbacks.load(std::memory_order_relaxed); }
 
 }  // extern "C"

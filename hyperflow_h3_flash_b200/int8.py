@@ -78,8 +78,9 @@ def regular_hadamard(group: int) -> Tensor:
 
 
 def hadamard_factors(group: int) -> tuple[int, int] | None:
-    """``(GA, GB)`` with ``regular_hadamard(group) == kron(regular_hadamard(GA), regular_hadamard(GB))``, both at
-    least 16; None otherwise (int8.py:112-119)."""
+    """Split of a group of 2^n channels (n even, group >= 256) into Hadamard sizes ``GA = 4^floor(n/4)`` and
+    ``GB = group / GA``, both 16 or more, whose Kronecker product is the group's matrix; ``None`` for any other
+    group (the factored rotation's precondition, int8.py:112-119)."""
     n = group.bit_length() - 1
     if group < 256 or group != 1 << n or n % 2:
         return None
@@ -110,7 +111,8 @@ class Int8RotLinear(nn.Module):
             raise ValueError(f"in_features {in_features} is not a multiple of the Hadamard group {group}")
         self.in_features, self.out_features, self.group = in_features, out_features, group
         self.keep_input = False
-        # Parameters, not buffers: diffusers' streamed group offloading moves module buffers on but never back off.
+        # Weights are registered as frozen nn.Parameters rather than buffers, so that offloading hooks which move a
+        # module's parameters between host and device treat them like every other weight of the model.
         self.qweight = nn.Parameter(torch.zeros(out_features, in_features, dtype=torch.int8), requires_grad=False)
         self.wscale = nn.Parameter(torch.ones(out_features, dtype=torch.float32), requires_grad=False)
         if bias:
@@ -130,7 +132,8 @@ class Int8RotLinear(nn.Module):
 
     def _quantize(self, x: Tensor, x2: Tensor, kernels: SimpleNamespace) -> tuple[Tensor, Tensor]:
         cache = Int8RotLinear._last_input
-        # Inference tensors (`torch.inference_mode`) have no version counter.
+        # A tensor made under torch.inference_mode() carries no _version (reading it raises), so it is keyed by
+        # identity alone: such tensors cannot be modified in place outside inference mode anyway.
         version = None if x.is_inference() else x._version
         hit = cache.get("x") is x and cache.get("version") == version and cache.get("group") == self.group
         quantized = cache["value"] if hit else kernels.rotate_quant(x2, self.group)

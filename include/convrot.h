@@ -71,7 +71,7 @@ int convrot_rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int g
 
 /*
  * Low-rank down projection alone: xa[m, j] = bf16(sum_k x[m,k] * lr_down[j,k]) (transformer.py:57-58).
- * A tcgen05 bf16 GEMM with an fp32 accumulator; r % 16 == 0, 16 <= r <= 256, K % 8 == 0.
+ * A tcgen05 bf16 GEMM with an fp32 accumulator; 1 <= r <= 256, K % 8 == 0, ldx / ld_down / ldxa multiples of 8.
  */
 int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down,
                          int64_t M, int64_t K, int64_t r, void* xa_out, int64_t ldxa, void* stream);
@@ -84,7 +84,8 @@ int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_
  *   bias bf16 [N] or NULL, xa bf16 [M, r] (ldxa) and lr_up bf16 [N, r] (ld_up, LowRankLinear.up.weight) or NULL,
  *   y bf16 [M, N] (ldy).
  * Without bias and low-rank the output is bitwise the reference's (int8.py:311, 324).
- * K % 16 == 0; ldq, ldw multiples of 16; ldy multiple of 8; r % 16 == 0 and r <= 256 when present.
+ * K % 16 == 0; ldq, ldw multiples of 16; ldy multiple of 8; 1 <= r <= 256 when present, with ldxa and ld_up
+ * multiples of 8 (a rank that is not a multiple of 8 is read through padded rows; the padding is never read).
  */
 int convrot_gemm(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* sx, const float* ws,
                  const void* bias, const void* xa, int64_t ldxa, const void* lr_up, int64_t ld_up, int64_t r,
@@ -216,7 +217,9 @@ int convrot_peer_signal(uint32_t* const* slots, int n, uint32_t epoch, void* str
 int convrot_peer_wait(const uint32_t* flags, int n, uint32_t epoch, void* stream);
 
 /*
- * Workspace for convrot_linear: q (int8 [M, K]), s (fp32 [M]) and xa (bf16 [M, r]), each 256-byte aligned.
+ * Workspace for convrot_linear: q (int8 [M, K] with rows padded to a multiple of 16 bytes), s (fp32 [M]) and xa
+ * (bf16 [M, r] with rows padded to a multiple of 8 elements), each 256-byte aligned.  Exactly the size
+ * convrot_linear requires; 0 for negative arguments.
  */
 size_t convrot_workspace_size(int64_t M, int64_t K, int64_t r);
 
@@ -240,7 +243,7 @@ int convrot_linear(const void* x, int64_t ldx, const int8_t* w, int64_t ldw, con
  * cudaFree or allocating library routine.
  *
  * Limit: the codes, scales and low-rank input of one call must fit CONVROT_NOALLOC_SCRATCH_BYTES (16 MiB), i.e.
- * convrot_workspace_size(M, K, r) rounded as convrot_linear rounds it (for example M = 3072 rows at K = 5120);
+ * convrot_workspace_size(M, K, r) <= 16 MiB (for example M = 3072 rows at K = 5120);
  * larger problems return CONVROT_ERR_SCRATCH without launching anything.  The scratch is part of the library's
  * device image: every GPU that loads the library holds those 16 MiB until the process exits.
  *
@@ -297,6 +300,14 @@ int convrot_set_rotate_tuning(int stages, int ctas_per_sm);
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 int convrot_version(void);
+
+/*
+ * How many low-rank down projections of this process ran without their K split (no counterpart in the reference).
+ * Down projections with M <= 1024 split K over a cluster of 2-8 CTAs; if the GPU cannot place such a cluster the
+ * launch runs the unsplit kernel instead, whose different fp32 summation order can change the last bf16 bit of xa
+ * (and so of the low-rank term).  Any other launch error is returned as CONVROT_ERR_CUDA, never absorbed.
+ */
+int64_t convrot_split_k_fallbacks(void);
 
 #ifdef __cplusplus
 }

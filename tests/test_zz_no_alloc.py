@@ -31,16 +31,28 @@ def _ptr(t):
     return None if t is None else P(t.data_ptr())
 
 
+def _up_padded(w, r):
+    """LowRankLinear.up's weight [N, r] with its rows padded to a multiple of 8 elements (the 16-byte rule of the
+    C ABI's leading dimensions), and that leading dimension."""
+    ld_up = -(-r // 8) * 8
+    if ld_up == r:
+        return w.up, r
+    up = torch.zeros(w.up.shape[0], ld_up, dtype=w.up.dtype, device=w.up.device)
+    up[:, :r] = w.up
+    return up, ld_up
+
+
 def _with_workspace(L, x, w, r, group):
     """The existing entry point: convrot_linear on a workspace allocated by the caller (here: torch)."""
     M, K = x.shape
     N = w.qweight.shape[0]
+    up, ld_up = _up_padded(w, r) if r else (None, 0)
     nbytes = L.convrot_workspace_size(M, K, r)
     ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=DEV)
     base = (ws.data_ptr() + 255) // 256 * 256
     y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
     rc = L.convrot_linear(_ptr(x), K, _ptr(w.qweight), K, _ptr(w.wscale), _ptr(w.bias),
-                          _ptr(w.down) if r else None, K, _ptr(w.up) if r else None, r, r, M, N, K, group,
+                          _ptr(w.down) if r else None, K, _ptr(up), ld_up, r, M, N, K, group,
                           P(base), nbytes, _ptr(y), N, P(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "convrot_linear")
     return y
@@ -49,19 +61,33 @@ def _with_workspace(L, x, w, r, group):
 def _no_alloc(L, x, w, r, group):
     M, K = x.shape
     N = w.qweight.shape[0]
+    up, ld_up = _up_padded(w, r) if r else (None, 0)
     y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
     rc = L.convrot_linear_noalloc(_ptr(x), K, _ptr(w.qweight), K, _ptr(w.wscale), _ptr(w.bias),
-                                  _ptr(w.down) if r else None, K, _ptr(w.up) if r else None, r, r, M, N, K, group,
+                                  _ptr(w.down) if r else None, K, _ptr(up), ld_up, r, M, N, K, group,
                                   _ptr(y), N, P(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "convrot_linear_noalloc")
     return y
 
 
+def _largest_rows_that_fit(L, K, r):
+    """The largest M whose codes, scales and low-rank input (convrot_workspace_size) fit the built-in scratch."""
+    lo, hi = 1, 1 << 20  # fits / does not fit
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        if L.convrot_workspace_size(mid, K, r) <= _lib.NOALLOC_SCRATCH_BYTES:
+            lo = mid
+        else:
+            hi = mid
+    return lo
+
+
 def test_no_alloc_entry_matches_the_workspace_entry_on_two_calls_in_a_row():
     L = _lib.lib()
-    cases = [  # (M, K, N, r, group, seed): the second call is smaller, so stale scratch would show
+    cases = [  # (M, K, N, r, group, seed): each call is smaller than the one before, so stale scratch would show
         (1000, 5120, 2048, 32, 256, 1),
         (333, 4096, 1536, 64, 256, 2),
+        (77, 1024, 512, 36, 256, 4),  # a rank that is not a multiple of 8 (xa rows padded inside the scratch)
     ]
     for M, K, N, r, group, seed in cases:
         x = synthetic.activations(M, K, seed=seed).to(DEV)
@@ -86,3 +112,22 @@ def test_no_alloc_entry_without_low_rank_and_its_size_limit():
     assert rc == _lib.ERR_SCRATCH
     assert "scratch" in _lib.status_string(rc)
     assert _lib.NOALLOC_SCRATCH_BYTES == 16 << 20
+
+
+def test_no_alloc_entry_at_the_edge_of_its_scratch():
+    """The largest problem that fits the scratch (K = 5120, r = 32) runs and equals the workspace entry bitwise;
+    one more row is rejected before anything is launched."""
+    L = _lib.lib()
+    K, N, r = 5120, 512, 32
+    M = _largest_rows_that_fit(L, K, r)
+    assert L.convrot_workspace_size(M + 1, K, r) > _lib.NOALLOC_SCRATCH_BYTES >= L.convrot_workspace_size(M, K, r)
+    x = synthetic.activations(M, K, seed=5).to(DEV)
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256, seed_offset=5).to(DEV)
+    got = _no_alloc(L, x, w, r, 256)
+    expected = _with_workspace(L, x, w, r, 256)
+    torch.cuda.synchronize()
+    assert torch.equal(got, expected)
+    rc = L.convrot_linear_noalloc(P(16), K, P(16), K, P(16), None, P(16), K, P(16), r, r, M + 1, N, K, 256, P(16),
+                                  N, None)
+    assert rc == _lib.ERR_SCRATCH
+    assert L.convrot_poll_error(None) == 0
