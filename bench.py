@@ -131,31 +131,110 @@ class ClockSampler:
 # --------------------------------------------------------------------------------------------------- CPU arm
 
 
-def cpu_port_linear_set(rows: int, steps: int, warmup: int) -> dict:
-    """The reference's CPU path for the linear set, ported to numpy/BLAS, on `rows` token rows."""
-    import numpy as np
+def host_threads() -> int:
+    """Every core this process may run on, set as the thread count of torch and of numpy's BLAS: torchrun exports
+    OMP_NUM_THREADS=1 to its children, which would otherwise leave the CPU arm on one core."""
+    cores = len(os.sched_getaffinity(0))
+    import torch
+
+    torch.set_num_threads(cores)
+    try:
+        import threadpoolctl
+
+        threadpoolctl.threadpool_limits(limits=cores)
+    except Exception:  # noqa: BLE001 - numpy then keeps its own default
+        pass
+    return cores
+
+
+def load_reference_int8():
+    """The reference's int8 module from its installed copy (baseline/_ref), loaded by file path: the package's
+    __init__ imports diffusers, which this path does not need.  Returns (module, None) or (None, why)."""
+    import importlib.util
+
+    path = os.path.join(ROOT, "baseline", "_ref", "hyperflow_h3_flash", "int8.py")
+    if not os.path.exists(path):
+        return None, "the reference is not installed under baseline/_ref"
+    try:
+        spec = importlib.util.spec_from_file_location("hyperflow_h3_flash_ref_int8", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    except Exception as e:  # noqa: BLE001 - reported as the reason
+        return None, f"loading baseline/_ref int8.py failed: {type(e).__name__}: {e}"
+    return mod, None
+
+
+def reference_layers(ref, torch, dev, K: int, N: int, rank: int, count: int, seed0: int = 0):
+    """`count` of the reference's own Int8RotLinear modules with the synthetic weights of this bench, plus their bias
+    and LowRankLinear factors (transformer.py:48-58: two bias-free bf16 nn.Linear), on `dev`."""
+    from hyperflow_h3_flash_b200 import synthetic
+
+    out = []
+    for i in range(count):
+        w = synthetic.linear_weights(K, N, rank=rank, bias=True, group=GROUP, seed_offset=seed0 + i)
+        layer = ref.Int8RotLinear(K, N, GROUP)
+        layer.qweight.data.copy_(w.qweight)
+        layer.wscale.data.copy_(w.wscale)
+        down = torch.nn.Linear(K, rank, bias=False, dtype=torch.bfloat16)
+        up = torch.nn.Linear(rank, N, bias=False, dtype=torch.bfloat16)
+        down.weight.data.copy_(w.down)
+        up.weight.data.copy_(w.up)
+        out.append((layer.to(dev), w.bias.to(dev), down.to(dev), up.to(dev)))
+    return out
+
+
+def reference_linear(x, parts):
+    """The reference's modules composed as this path computes: Int8RotLinear(x) + bias + up(down(x)), bf16 ops."""
+    layer, bias, down, up = parts
+    return layer(x) + bias + up(down(x))
+
+
+def cpu_linear_set(rows: int, steps: int, warmup: int) -> dict:
+    """The reference's CPU path for the linear set on `rows` token rows, on every host core: its own
+    Int8RotLinear on CPU tensors (_forward_torch, int8.py:173-179) from the installed copy, plus bias and
+    up(down(x)); the numpy/BLAS port in oracle/ when the copy is absent.  Median seconds per step."""
     import torch
 
     from hyperflow_h3_flash_b200 import synthetic
-    from oracle import oracle as O
 
-    cores = len(os.sched_getaffinity(0))
-    x = synthetic.activations(rows, K_DIM).view(torch.int16).numpy().view(np.uint16)
-    layers = [synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=i)
-              for i in range(4)]
-    h = O.regular_hadamard(GROUP)
+    cores = host_threads()
+    ref, why = load_reference_int8()
+    x = synthetic.activations(rows, K_DIM)
+    if ref is not None:
+        kind = "reference"
+        parts = reference_layers(ref, torch, torch.device("cpu"), K_DIM, N_DIM, RANK, 4)
 
-    def linear(xb, w):
-        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
-        y = O.bf16_to_f32(O.forward_cpu_port(xb, w.qweight.numpy(), w.wscale.numpy(), GROUP, h))
-        y = O.bf16_to_f32(O.f32_to_bf16(y + O.bf16_to_f32(bits(w.bias))[None, :]))
-        xa = O.f32_to_bf16(O.bf16_to_f32(xb) @ O.bf16_to_f32(bits(w.down)).T)
-        lr = O.f32_to_bf16(O.bf16_to_f32(xa) @ O.bf16_to_f32(bits(w.up)).T)
-        return O.f32_to_bf16(y + O.bf16_to_f32(lr))
+        def step():
+            with torch.inference_mode():
+                q, k, v = (reference_linear(x, parts[i]) for i in range(3))
+                return reference_linear(v, parts[3])
 
-    def step():
-        q, k, v = (linear(x, layers[i]) for i in range(3))
-        return linear(v, layers[3])
+        what = ("the reference's Int8RotLinear.forward on CPU tensors (_forward_torch, int8.py:173-179, from "
+                "baseline/_ref) + bias + LowRankLinear, torch")
+    else:
+        import numpy as np
+
+        from oracle import oracle as O
+
+        kind = "port"
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        layers = [synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=i)
+                  for i in range(4)]
+        h = O.regular_hadamard(GROUP)
+
+        def linear(xv, w):
+            bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+            y = O.bf16_to_f32(O.forward_cpu_port(xv, w.qweight.numpy(), w.wscale.numpy(), GROUP, h))
+            y = O.bf16_to_f32(O.f32_to_bf16(y + O.bf16_to_f32(bits(w.bias))[None, :]))
+            xa = O.f32_to_bf16(O.bf16_to_f32(xv) @ O.bf16_to_f32(bits(w.down)).T)
+            lr = O.f32_to_bf16(O.bf16_to_f32(xa) @ O.bf16_to_f32(bits(w.up)).T)
+            return O.f32_to_bf16(y + O.bf16_to_f32(lr))
+
+        def step():
+            q, k, v = (linear(xb, layers[i]) for i in range(3))
+            return linear(v, layers[3])
+
+        what = f"numpy/BLAS port of _forward_torch (oracle/) + bias + up(down(x)) ({why})"
 
     for _ in range(warmup):
         step()
@@ -166,11 +245,14 @@ def cpu_port_linear_set(rows: int, steps: int, warmup: int) -> dict:
         times.append(time.perf_counter() - t0)
     ops = 4 * 2.0 * rows * K_DIM * N_DIM
     t = statistics.median(times)
-    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
-            "sample": f"{rows} token rows of the linear set (4 linears {K_DIM}x{N_DIM}, r={RANK}, bias), "
-                      f"median of {steps} after {warmup} warm-up, numpy/BLAS port of _forward_torch "
-                      f"(int8.py:173-179) + bias + up(down(x))",
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": kind,
+            "sample": f"{rows} token rows of the linear set (4 linears {K_DIM}x{N_DIM}, r={RANK}, bias; q/k/v on x, "
+                      f"out on v), median of {steps} steps after {warmup} warm-up, {cores} threads: {what}",
             "seconds_per_step": t, "mean_seconds_per_step": statistics.mean(times)}
+
+
+#: The CPU sample of both arms: rows per step (about 0.5 s of CPU work per step on 32 cores) and warm-up steps.
+CPU_ROWS, CPU_WARMUP = 1024, 1
 
 
 METRIC = 'INT8 convrot linear TOPS & % dense-INT8 peak; DiT-block linear-set ms at 1/2/4/8 B200'
@@ -199,8 +281,7 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    rows = 1024
-    res = cpu_port_linear_set(rows, args.steps, args.warmup)
+    res = cpu_linear_set(CPU_ROWS, args.steps, max(CPU_WARMUP, args.warmup))
     line = {
         "metric": METRIC, "metric_detail": METRIC_DETAIL, "value": res["value"],
         "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -431,7 +512,7 @@ def run_ours(args) -> None:
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_extras:
-            cpu = cpu_port_linear_set(2048, 3, 1)
+            cpu = cpu_linear_set(CPU_ROWS, 5, CPU_WARMUP)
             cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
         line = {
             "metric": METRIC,
@@ -524,6 +605,95 @@ def pipelined_e2e(torch, dev, step, x_host, y_host, args, barrier) -> float:
     return start.elapsed_time(end)
 
 
+def reference_gpu_path(torch, I, dev, x, steps: int) -> dict:
+    """The reference's own B200 path beside this one, on the same seeded config-2 inputs (N = 1):
+
+    * parity: its Triton rotate_quant kernels (factored, the pipeline default, pipeline.py:232; and dense,
+      int8.py:194-262) against this library's codes and scales; torch._int_mm's int32 accumulator (its B200 GEMM,
+      int8.py:353-364) and its int8_matmul output (cuBLASLt + Triton rescale) against this library's on the same
+      codes;
+    * time: its linear set (Int8RotLinear with the q/k/v keep_input sharing, + bias + LowRankLinear in bf16 torch
+      ops) and its parts, CUDA events over `steps` calls after 3 warm-up calls.
+    """
+    ref, why = load_reference_int8()
+    if ref is None:
+        return {"unavailable": why}
+    try:
+        kernels = ref._kernels()
+    except Exception as e:  # noqa: BLE001 - reported
+        return {"unavailable": f"the reference's _kernels() failed: {type(e).__name__}: {e}"}
+    if kernels is None:
+        return {"unavailable": "Triton is not importable, so the reference has no CUDA kernels (int8.py:182-188)"}
+    M = x.shape[0]
+    out = {"source": "baseline/_ref/hyperflow_h3_flash/int8.py loaded by file path; kernel options as "
+                     "load_pipeline's defaults (int8_gemm auto -> cublas on sm_100, rotate_quant factored) unless named",
+           "resolved_int8_gemm": ref.resolve_int8_gemm(dev)}
+    parts = reference_layers(ref, torch, dev, K_DIM, N_DIM, RANK, 4)
+    layer0 = parts[0][0]
+    q, s = I.rotate_quant(x, GROUP)
+    parity = {}
+    for opt in ("factored", "dense"):
+        ref.set_kernel_options(rotate_quant=opt)
+        qr, sr = kernels.rotate_quant(x, GROUP)
+        torch.cuda.synchronize()
+        dq = (qr.to(torch.int16) - q.to(torch.int16)).abs()
+        su, sru = s.view(torch.int32).long(), sr.view(torch.int32).long()
+        parity[f"rotate_quant_{opt}"] = {
+            "codes_equal_frac": float((dq == 0).double().mean()), "codes_max_abs_diff": int(dq.max()),
+            "codes_differing": int((dq != 0).sum()), "codes_total": dq.numel(),
+            "scales_equal_frac": float((su == sru).double().mean()),
+            "scales_max_ulp_diff": int((su - sru).abs().max()),
+        }
+        del qr, sr, dq
+    acc_ours = I.int8_mm_acc(q, layer0.qweight)
+    acc_ref = torch._int_mm(q, layer0.qweight.t())
+    parity["int32_accumulator_bitwise_equal"] = bool(torch.equal(acc_ours, acc_ref))
+    del acc_ours, acc_ref
+    y_ours = I.int8_matmul(q, layer0.qweight, s, layer0.wscale)
+    y_ref = kernels.int8_matmul(q, layer0.qweight, s, layer0.wscale)
+    parity["int8_matmul_output_bitwise_equal"] = bool(torch.equal(y_ours, y_ref))
+    del y_ours, y_ref
+    out["parity_cfg2"] = parity
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(steps):
+            fn()
+        en.record()
+        en.synchronize()
+        return st.elapsed_time(en) / steps
+
+    to_q, to_k = parts[0][0], parts[1][0]
+
+    def linear_set():
+        to_q.keep_input = to_k.keep_input = True
+        q_, k_, v_ = (reference_linear(x, parts[i]) for i in range(3))
+        return reference_linear(v_, parts[3])
+
+    ops = 4 * 2.0 * M * K_DIM * N_DIM
+    times = {}
+    with torch.inference_mode():
+        for opt in ("factored", "dense"):
+            ref.set_kernel_options(rotate_quant=opt)
+            ms = timed(linear_set)
+            times[f"linear_set_{opt}"] = {"ms": ms, "tops": ops / (ms * 1e-3) / 1e12}
+            times[f"rotate_quant_{opt}_ms"] = timed(lambda: kernels.rotate_quant(x, GROUP))
+        ref.set_kernel_options(rotate_quant="factored")
+        times["int8_matmul_ms"] = timed(lambda: kernels.int8_matmul(q, layer0.qweight, s, layer0.wscale))
+        down, up = parts[0][2], parts[0][3]
+        times["lowrank_up_down_ms"] = timed(lambda: up(down(x)))
+    to_q.keep_input = to_k.keep_input = False
+    ref.Int8RotLinear._last_input.clear()
+    out["time_cfg2"] = times
+    out["ms_per_step"] = times["linear_set_factored"]["ms"]
+    out["tops"] = times["linear_set_factored"]["tops"]
+    return out
+
+
 def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     """Config 2's single linear, config 3's block set, rotate+quantise bandwidth (N = 1 only)."""
     out = {}
@@ -552,6 +722,7 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
         return {n: sorted(v)[len(v) // 2] for n, v in samples.items()}
 
     M = args.rows
+    out["reference_gpu"] = reference_gpu_path(torch, I, dev, x, args.steps)
     w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=7)
     layer = I.Int8RotLinear(K_DIM, N_DIM, GROUP, bias=True, rank=RANK)
     synthetic.load_into(layer, w)

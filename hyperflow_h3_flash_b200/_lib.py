@@ -15,7 +15,7 @@ from .build import LIB
 # Status codes (include/convrot.h).
 OK, ERR_SHAPE, ERR_GROUP, ERR_ALIGN, ERR_CUDA, ERR_ARCH, ERR_TIMEOUT, ERR_ARG, ERR_SCRATCH = range(9)
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ROUND_KERNEL, ROUND_TORCH = 0, 1
+ROUND_KERNEL, ROUND_TORCH, ROUND_TRITON = 0, 1, 2
 
 _P, _I, _L, _S, _U64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_uint64
 _U32 = ctypes.c_uint32

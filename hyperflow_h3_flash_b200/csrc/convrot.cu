@@ -365,7 +365,9 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   if (has_lr) {
     if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r * lr_segments, ldxa, kBM, lr_atom / 2)))
       return rc;
-    if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, b_rows, lr_atom / 2))) return rc;
+    // up rows per load: the 1-SM tile's 256, or the 2-SM CTA's 64-row share of one 128-column half
+    const int up_rows = two_sm ? 64 : b_rows;
+    if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, up_rows, lr_atom / 2))) return rc;
   }
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -466,6 +468,14 @@ int lowrank_down(const void* x, int64_t ldx, const void* down, int64_t ld_down, 
 
 // ---------------------------------------------------------------------------------------------- rotate+quant
 
+using RotQuantKernel = void (*)(const RotQuantParams);
+
+// The instance of a rotate kernel for a rounding mode (CONVROT_ROUND_KERNEL / _TORCH / _TRITON).
+RotQuantKernel by_rounding(int rounding, RotQuantKernel kernel_mode, RotQuantKernel torch_mode,
+                           RotQuantKernel triton_mode) {
+  return rounding == CONVROT_ROUND_TORCH ? torch_mode : rounding == CONVROT_ROUND_TRITON ? triton_mode : kernel_mode;
+}
+
 template <int G>
 int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t stream) {
   const int nslots = p.K / 16;
@@ -477,11 +487,13 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
   RotQuantParams q = p;
   cudaError_t e;
   void (*kernel)(const RotQuantParams) = nullptr;
-  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
   switch (slots) {
-    case 1: kernel = torch_rounding ? rotate_quant_kernel<G, 1, 1> : rotate_quant_kernel<G, 1, 0>; break;
-    case 2: kernel = torch_rounding ? rotate_quant_kernel<G, 2, 1> : rotate_quant_kernel<G, 2, 0>; break;
-    default: kernel = torch_rounding ? rotate_quant_kernel<G, 4, 1> : rotate_quant_kernel<G, 4, 0>; break;
+    case 1: kernel = by_rounding(p.rounding, rotate_quant_kernel<G, 1, 0>, rotate_quant_kernel<G, 1, 1>,
+                                 rotate_quant_kernel<G, 1, 2>); break;
+    case 2: kernel = by_rounding(p.rounding, rotate_quant_kernel<G, 2, 0>, rotate_quant_kernel<G, 2, 1>,
+                                 rotate_quant_kernel<G, 2, 2>); break;
+    default: kernel = by_rounding(p.rounding, rotate_quant_kernel<G, 4, 0>, rotate_quant_kernel<G, 4, 1>,
+                                  rotate_quant_kernel<G, 4, 2>); break;
   }
   int regs = -1;  // the kernel's registers per thread, cached with the shared-memory opt-in
   int rc = cached_resident(reinterpret_cast<const void*>(kernel), &regs);
@@ -536,18 +548,22 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   const bool adaln = p.mod_scale != nullptr;
   if (adaln && (chunked || slots != 1)) return CONVROT_ERR_SHAPE;
   if (chunked && slots == 1 && threads > kRQ256ChunkedThreads) return launch_rq<256>(st, p, stream);
-  const bool torch_rounding = p.rounding == CONVROT_ROUND_TORCH;
   void (*kernel)(const RotQuantParams) = nullptr;
   if (adaln)
-    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, false, true> : rotate_quant256_kernel<1, 0, false, true>;
+    kernel = by_rounding(p.rounding, rotate_quant256_kernel<1, 0, false, true>,
+                         rotate_quant256_kernel<1, 1, false, true>, rotate_quant256_kernel<1, 2, false, true>);
   else if (slots == 1 && !chunked)
-    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, false> : rotate_quant256_kernel<1, 0, false>;
+    kernel = by_rounding(p.rounding, rotate_quant256_kernel<1, 0, false>, rotate_quant256_kernel<1, 1, false>,
+                         rotate_quant256_kernel<1, 2, false>);
   else if (slots == 1)
-    kernel = torch_rounding ? rotate_quant256_kernel<1, 1, true> : rotate_quant256_kernel<1, 0, true>;
+    kernel = by_rounding(p.rounding, rotate_quant256_kernel<1, 0, true>, rotate_quant256_kernel<1, 1, true>,
+                         rotate_quant256_kernel<1, 2, true>);
   else if (!chunked)
-    kernel = torch_rounding ? rotate_quant256_kernel<2, 1, false> : rotate_quant256_kernel<2, 0, false>;
+    kernel = by_rounding(p.rounding, rotate_quant256_kernel<2, 0, false>, rotate_quant256_kernel<2, 1, false>,
+                         rotate_quant256_kernel<2, 2, false>);
   else
-    kernel = torch_rounding ? rotate_quant256_kernel<2, 1, true> : rotate_quant256_kernel<2, 0, true>;
+    kernel = by_rounding(p.rounding, rotate_quant256_kernel<2, 0, true>, rotate_quant256_kernel<2, 1, true>,
+                         rotate_quant256_kernel<2, 2, true>);
   int regs = -1;  // the kernel's registers per thread, cached with the shared-memory opt-in
   int rc = cached_resident(reinterpret_cast<const void*>(kernel), &regs);
   if (rc) return rc;
@@ -606,7 +622,8 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
     return CONVROT_ERR_ARG;  // a plain row-major x is already what x_out would hold
   }
   if (group != 4 && group != 16 && group != 64 && group != 256) return CONVROT_ERR_GROUP;
-  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
+  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH && rounding != CONVROT_ROUND_TRITON)
+    return CONVROT_ERR_ARG;
   if (K % group || K % 16 || K > 32768 || ldx < x_chunk || ldq < K || M > INT32_MAX) return CONVROT_ERR_SHAPE;
   if (x_out && ld_out < K) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;
@@ -656,7 +673,8 @@ int rotate_quant_adaln(const void* x, int64_t ldx, int64_t M, int64_t K, int gro
   if (group != 256) return CONVROT_ERR_GROUP;
   if (M < 0 || K <= 0 || K % 256 || K > 8192 || ldx < K || ldq < K || ld_mod < K || M > INT32_MAX)
     return CONVROT_ERR_SHAPE;
-  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH) return CONVROT_ERR_ARG;
+  if (rounding != CONVROT_ROUND_KERNEL && rounding != CONVROT_ROUND_TORCH && rounding != CONVROT_ROUND_TRITON)
+    return CONVROT_ERR_ARG;
   if (!(eps >= 0.0f)) return CONVROT_ERR_ARG;
   if (h_out && ld_h < K) return CONVROT_ERR_SHAPE;
   if (M == 0) return CONVROT_OK;

@@ -12,9 +12,15 @@
 //   warps 2..5  epilogue over this CTA's 128 accumulator rows (as in the 1-SM kernel)
 //   warp 6      TMA producer of this CTA's low-rank tiles (xa rows, up rows)
 //
-// Cross-CTA signalling uses plain (non-multicast) operations only: TMA loads complete on the leader's barrier
-// through its cluster address, the leader commits MMA completion once per CTA, and the peer's epilogue arrives on
-// the leader's barriers remotely (mapa).  Every wait is bounded as in the 1-SM kernel.
+// Cross-CTA signalling: TMA loads (never multicast: each CTA fetches its own bytes) complete on the leader's barrier
+// through its cluster address, the leader signals MMA completion to both CTAs' barriers with one tcgen05.commit,
+// and the peer's epilogue arrives on the leader's barriers remotely (mapa).  Every wait is bounded as in the 1-SM
+// kernel.
+//
+// With the low-rank term the epilogue works per 128-column half of its accumulator: it reads and dequantises the
+// half into registers, the leader then runs the half's kind::f16 MMA xa . up^T (M = 256, N = 128, accumulate = 0)
+// over those TMEM columns, and the epilogue adds the product to the held values.  No fp32 value is written back to
+// TMEM.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -117,6 +123,17 @@ __device__ __forceinline__ void mma_commit_pair(uint32_t cluster_addr) {
                : "memory");
 }
 
+// The same arrival on the barrier at this shared-memory offset in BOTH CTAs of the pair, as one commit (an MMA
+// completion signal, not a data copy).  Measured on B200: one commit per stage instead of two shortens the MMA
+// issue of a 256 x 256 x 5120 tile from 23.8k to 22.1k cycles.
+__device__ __forceinline__ void mma_commit_pair_both(uint32_t smem_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_addr),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
 template <int STAGES, int LR_ATOM, int LR_ATOMS>
 struct Gemm2Cfg {
   static constexpr int kBN = 256;             // output columns per pair tile (= per CTA accumulator)
@@ -127,11 +144,14 @@ struct Gemm2Cfg {
   static constexpr int kBBytes = kBHalf * kRowBytes;   // 16 KB
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kLRXaBytes = kHasLR ? kBM * LR_ATOM * LR_ATOMS : 0;
-  static constexpr int kLRUpBytes = kHasLR ? kBHalf * LR_ATOM * LR_ATOMS : 0;
+  // The low-rank term runs per 128-column half of the tile: this CTA's share of one half's up rows is 64 rows.
+  static constexpr int kLRUpRows = 64;
+  static constexpr int kLRUpBytes = kHasLR ? kLRUpRows * LR_ATOM * LR_ATOMS : 0;
   static constexpr int kTmemCols = 512;
   static constexpr int kThreads = kHasLR ? 224 : 192;
-  // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2], lr_done[2], lr_full, lr_empty, drain
-  static constexpr int kNumBars = 2 * STAGES + 8 + 3;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2 x 2], lr_done[2 x 2], lr_full, lr_empty, drain
+  // (epi_ready and lr_done per accumulator buffer and 128-column half)
+  static constexpr int kNumBars = 2 * STAGES + 12 + 3;
   static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
   // Output staging: per epilogue warp two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B) for TMA stores.
   static constexpr int kStoreBoxBytes = 32 * 64;
@@ -141,7 +161,7 @@ struct Gemm2Cfg {
       1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kStoreBytes + kBarBytes + kSiluTableBytes;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory above the sm_100 per-CTA limit");
   static constexpr uint32_t kIdesc = make_idesc_i8(256, 256);
-  static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 256);
+  static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 128);  // one 128-column half per low-rank MMA
 };
 
 // One bf16 output map per column chunk (box 32 x 32): chunk j covers columns [j W, (j + 1) W) of the result.
@@ -168,11 +188,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* empty = bars + S;
   uint64_t* tmem_full = bars + 2 * S;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* epi_ready = tmem_full + 4;
-  uint64_t* lr_done = tmem_full + 6;
-  uint64_t* lr_full = tmem_full + 8;
-  uint64_t* lr_empty = tmem_full + 9;
-  uint64_t* drain = tmem_full + 10;
+  uint64_t* epi_ready = tmem_full + 4;  // [buf * 2 + half]
+  uint64_t* lr_done = tmem_full + 8;    // [buf * 2 + half]
+  uint64_t* lr_full = tmem_full + 12;
+  uint64_t* lr_empty = tmem_full + 13;
+  uint64_t* drain = tmem_full + 14;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint16_t* silu_tab = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + Cfg::kBarBytes);
@@ -197,6 +217,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&epi_ready[b], 8);
       mbar_init(&lr_done[b], 1);
     }
@@ -272,47 +294,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int pending_lr = -1;       // local tile index whose low-rank MMA is not issued yet
-      int pending_chunk = 0;     // its next rank chunk
-      bool lr_epi_seen = false;  // both CTAs' epilogue pass 1 is done for it
+      int pending_half = 0;      // its next 128-column half
+      int pending_chunk = 0;     // that half's next rank chunk
+      bool lr_epi_seen = false;  // both CTAs' epilogues have read that half's accumulator
       uint32_t lr_full_phase = 0;
       const uint32_t ring_base = smem_u32(ring);
       const uint32_t xa_base = smem_u32(lr_xa);
       const uint32_t up_base = smem_u32(lr_up);
-      const uint32_t empty_self = smem_u32(empty), empty_peer = mapa_shared(empty_self, 1);
-      const uint32_t tfull_self = smem_u32(tmem_full), tfull_peer = mapa_shared(tfull_self, 1);
-      const uint32_t lrdone_self = smem_u32(lr_done), lrdone_peer = mapa_shared(lrdone_self, 1);
-      const uint32_t lrempty_self = smem_u32(lr_empty), lrempty_peer = mapa_shared(lrempty_self, 1);
-      // One rank chunk of the low-rank MMA of local tile j (both CTAs' halves); the last also signals the epilogues.
-      auto issue_lr_chunk = [&](int j, bool last) {
-        const uint32_t d = tmem_base + (j & 1) * BN;
+      const uint32_t empty_self = smem_u32(empty);
+      const uint32_t tfull_self = smem_u32(tmem_full);
+      const uint32_t lrdone_self = smem_u32(lr_done);
+      const uint32_t lrempty_self = smem_u32(lr_empty);
+      // One rank chunk of the low-rank MMA of 128-column half h of local tile j (both CTAs' rows).  The half's
+      // first MMA overwrites its accumulator columns (the epilogue has read the int32 values and holds them
+      // dequantised in registers), so the product lands in TMEM on its own; the half's last chunk tells both CTAs'
+      // epilogues.
+      auto issue_lr_chunk = [&](int j, int h, int c, bool last) {
+        const uint32_t d = tmem_base + (j & 1) * BN + h * (BN / 2);
         for (int a = 0; a < LR_ATOMS; ++a) {
           for (int off = 0; off < LR_ATOM; off += 32) {
             const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
-            const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kBHalf * LR_ATOM + off, LR_ATOM);
-            mma_f16_pair(d, ad, bd, Cfg::kIdescLR, 1u);
+            const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kLRUpRows * LR_ATOM + off, LR_ATOM);
+            mma_f16_pair(d, ad, bd, Cfg::kIdescLR, (c | a | off) != 0);
           }
         }
-        if (last) {
-          mma_commit_pair(lrdone_self + (j & 1) * 8);
-          mma_commit_pair(lrdone_peer + (j & 1) * 8);
-        }
-        mma_commit_pair(lrempty_self);
-        mma_commit_pair(lrempty_peer);
+        if (last) mma_commit_pair_both(lrdone_self + ((j & 1) * 2 + h) * 8);
+        mma_commit_pair_both(lrempty_self);
       };
       auto lr_step = [&]() {
         tc_fence_after();
         const bool last = pending_chunk + 1 == lr_chunks;
-        issue_lr_chunk(pending_lr, last);
+        issue_lr_chunk(pending_lr, pending_half, pending_chunk, last);
         lr_full_phase ^= 1;
-        if (last)
-          pending_lr = -1;
-        else
+        if (!last) {
           ++pending_chunk;
+        } else if (pending_half == 0) {
+          pending_half = 1;
+          pending_chunk = 0;
+          lr_epi_seen = false;
+        } else {
+          pending_lr = -1;
+        }
       };
+      auto lr_epi_bar = [&]() { return &epi_ready[(pending_lr & 1) * 2 + pending_half]; };
       auto try_lr = [&]() {
         if (!HAS_LR || pending_lr < 0) return;
         if (!lr_epi_seen) {
-          if (!mbar_test_wait_cluster(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
+          if (!mbar_test_wait_cluster(lr_epi_bar(), (pending_lr >> 1) & 1)) return;
           lr_epi_seen = true;
         }
         if (!mbar_test_wait(lr_full, lr_full_phase)) return;
@@ -321,8 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       auto flush_lr = [&]() -> bool {
         while (HAS_LR && pending_lr >= 0) {
           if (!lr_epi_seen) {
-            if (!mbar_wait_cluster_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
-              return false;
+            if (!mbar_wait_cluster_bounded(lr_epi_bar(), (pending_lr >> 1) & 1, limit, abort_flag)) return false;
             lr_epi_seen = true;
           }
           if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
@@ -360,8 +387,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
           const uint64_t bd = make_kmajor_desc(a_addr + Cfg::kABytes, kRowBytes);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_i8_pair(d, ad + 2 * kk, bd + 2 * kk, Cfg::kIdesc, (kb | kk) != 0);
-          mma_commit_pair(empty_self + stage * 8);
-          mma_commit_pair(empty_peer + stage * 8);
+          mma_commit_pair_both(empty_self + stage * 8);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -369,14 +395,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
           if (HAS_LR) try_lr();
         }
         if (!ok) break;
-        mma_commit_pair(tfull_self + buf * 8);
-        mma_commit_pair(tfull_peer + buf * 8);
+        mma_commit_pair_both(tfull_self + buf * 8);
         if (HAS_LR) {
           if (!flush_lr()) {
             ok = false;
             break;
           }
           pending_lr = i;
+          pending_half = 0;
           pending_chunk = 0;
           lr_epi_seen = false;
         }
@@ -390,26 +416,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   } else if (HAS_LR && warp == 6) {
     // ------------------------------------------------------------ TMA producer: low-rank tiles of this CTA
     if (lane == 0) {
-      int u = 0;  // rank chunks loaded so far (all tiles)
+      int u = 0;  // rank-chunk loads so far (all tiles, both halves)
       bool ok = true;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kBHalf;
-        for (int c = 0; c < lr_chunks; ++c, ++u) {
-          // load u reuses the operand buffers once the MMA of load u-1 (phase u-1 of lr_empty) is done
-          if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
-            fail();
-            ok = false;
-            break;
-          }
-          if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
-          const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
-          for (int a = 0; a < LR_ATOMS; ++a) {
-            const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
-            tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x + xs, m0);
-            tma_load_2d_pair(lr_up + a * Cfg::kBHalf * LR_ATOM, &tmap_up, leader_lr_full, x, n0);
+        const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
+        // Per 128-column half h, this CTA holds up rows [128 h + 64 rank, + 64) of the tile (the pair's N = 128
+        // MMA splits its B operand between the two CTAs), and the xa rows of its 128 accumulator rows.
+        for (int h = 0; ok && h < 2; ++h) {
+          const int n0 = nb * BN + h * (BN / 2) + static_cast<int>(rank) * Cfg::kLRUpRows;
+          for (int c = 0; c < lr_chunks; ++c, ++u) {
+            // load u reuses the operand buffers once the MMA of load u-1 (phase u-1 of lr_empty) is done
+            if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
+              fail();
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(lr_full, 2 * (Cfg::kLRXaBytes + Cfg::kLRUpBytes));
+            for (int a = 0; a < LR_ATOMS; ++a) {
+              const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
+              tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x + xs, m0);
+              tma_load_2d_pair(lr_up + a * Cfg::kLRUpRows * LR_ATOM, &tmap_up, leader_lr_full, x, n0);
+            }
           }
         }
       }
@@ -471,7 +501,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
-      if (EPI == EPI_DEQUANT) {
+      if (EPI == EPI_DEQUANT && HAS_LR) {
+        // Per 128-column half: read the int32 accumulators and hold the dequantised values (+ bias) in registers,
+        // tell the MMA issuer that the half's columns are free, and wait while the low-rank MMA writes its product
+        // xa . up^T over them (accumulate = 0); then y = held + product, rounded once to bf16 on the way out.
+        const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+        uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
+        bool lr_ok = true;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          float hold[BN / 2];
+#pragma unroll
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int c = h * (BN / 2) + cc * 32;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            float t[32];
+            dequant_chunk(v, sa, p.sb, p.bias, n0 + c, p.N, t);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) hold[cc * 32 + j] = t[j];
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(leader_epi_ready0 + (buf * 2 + h) * 8);
+          if (!mbar_wait_bounded(&lr_done[buf * 2 + h], par, limit, abort_flag)) {
+            lr_ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int c = h * (BN / 2) + cc * 32;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            float t[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) t[j] = __fadd_rn(hold[cc * 32 + j], __uint_as_float(v[j]));
+            if (!p.swiglu) {
+              if (p.res && row_ok) gated_residual(t, p, row, n0 + c);
+              stage_and_store(t, m0 + quad * 32, n0 + c);  // rows beyond M are clipped by the TMA store
+            } else if (swiglu_block(t, c, ya, silu_tab)) {
+              stage_and_store(t, m0 + quad * 32, (n0 + c - 32) >> 1);
+            }
+          }
+        }
+        if (!lr_ok) {
+          fail();
+          break;
+        }
+      } else if (EPI == EPI_DEQUANT) {
         const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
         uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
 #pragma unroll 1
@@ -482,41 +562,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
           const int n = n0 + c;
           float t[32];
           dequant_chunk(v, sa, p.sb, p.bias, n, p.N, t);
-          if (HAS_LR) {
-            uint32_t w[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
-            tmem_st_32x32b_x32(taddr + c, w);
-          } else if (!p.swiglu) {
+          if (!p.swiglu) {
             if (p.res && row_ok) gated_residual(t, p, row, n);
             stage_and_store(t, m0 + quad * 32, n);  // rows beyond M are clipped by the TMA store
           } else if (swiglu_block(t, c, ya, silu_tab)) {
             stage_and_store(t, m0 + quad * 32, (n - 32) >> 1);
-          }
-        }
-        if (HAS_LR) {
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_remote(leader_epi_ready0 + buf * 8);
-          if (!mbar_wait_bounded(&lr_done[buf], par, limit, abort_flag)) {
-            fail();
-            break;
-          }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(taddr + c, v);
-            tmem_ld_wait();
-            float t[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            if (!p.swiglu) {
-              if (p.res && row_ok) gated_residual(t, p, row, n0 + c);
-              stage_and_store(t, m0 + quad * 32, n0 + c);
-            } else if (swiglu_block(t, c, ya, silu_tab))
-              stage_and_store(t, m0 + quad * 32, (n0 + c - 32) >> 1);
           }
         }
       } else {  // EPI_RAW_I32

@@ -78,6 +78,22 @@ __device__ __forceinline__ void h16_int(double (&v)[16]) {
   for (int l = 0; l < 4; ++l) h4_int(v[l], v[4 + l], v[8 + l], v[12 + l]);
 }
 
+// The per-token scale and its inverse from the row's amax (int8.py:212-214):
+//   s = max(amax, 1e-12) / 127,  inv = 1 / s.
+// Modes 0 (kernel) and 1 (torch path) divide with IEEE round-to-nearest, as the reference's source and its CPU path
+// state.  Mode 2 divides with PTX div.full.f32, the full-range approximate division (within 2 ulp) that the
+// reference's Triton kernels compile `/` to, so that codes and scales follow its B200 kernels bit for bit.
+template <int ROUNDING>
+__device__ __forceinline__ void scale_and_inverse(float amax, float& scale, float& inv) {
+  if constexpr (ROUNDING == 2) {
+    asm("div.full.f32 %0, %1, %2;" : "=f"(scale) : "f"(fmaxf(amax, 1e-12f)), "f"(127.0f));
+    asm("div.full.f32 %0, %1, %2;" : "=f"(inv) : "f"(1.0f), "f"(scale));
+  } else {
+    scale = __fdiv_rn(fmaxf(amax, 1e-12f), 127.0f);
+    inv = __fdiv_rn(1.0f, scale);
+  }
+}
+
 __device__ __forceinline__ uint32_t pack4_codes(float a, float b, float c, float d) {
   // |a..d| < 127.5: adding 1.5 * 2^23 rounds to an integer (half to even) and leaves the two's-complement code in
   // the low byte.
@@ -255,7 +271,7 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float f;
-        if constexpr (ROUNDING == 0)
+        if constexpr (ROUNDING != 1)
           f = __double2float_rn(v[j]);
         else
           f = __bfloat162float(__double2bfloat16(v[j]));
@@ -275,9 +291,10 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
     }
     float rmax = 0.0f;
     for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
-    const float scale = __fdiv_rn(fmaxf(__fmul_rn(rmax, kScale), 1e-12f), 127.0f);
+    float scale, inv;
+    scale_and_inverse<ROUNDING>(__fmul_rn(rmax, kScale), scale, inv);
     // y * inv = Yf * (inv * 2^-L) and y / s = Yf / (s * 2^L): the power-of-two factors are exact
-    const float inv_y = __fmul_rn(__fdiv_rn(1.0f, scale), kScale);
+    const float inv_y = __fmul_rn(inv, kScale);
     const float scale_y = __fdiv_rn(scale, kScale);
     int8_t* qrow = p.q + static_cast<int64_t>(m) * p.ldq;
 #pragma unroll
@@ -289,7 +306,7 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
       float t[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        if constexpr (ROUNDING == 0)
+        if constexpr (ROUNDING != 1)
           t[j] = __fmul_rn(y[sl][j], inv_y);
         else
           t[j] = __fdiv_rn(y[sl][j], scale_y);
@@ -568,7 +585,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           float f;
-          if constexpr (ROUNDING == 0)
+          if constexpr (ROUNDING != 1)
             f = __double2float_rn(v[h][j]);
           else
             f = __bfloat162float(__double2bfloat16(v[h][j]));
@@ -596,8 +613,9 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     }
     float rmax = 0.0f;
     for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
-    const float scale = __fdiv_rn(fmaxf(__fmul_rn(rmax, kScale), 1e-12f), 127.0f);
-    const float inv_y = __fmul_rn(__fdiv_rn(1.0f, scale), kScale);
+    float scale, inv;
+    scale_and_inverse<ROUNDING>(__fmul_rn(rmax, kScale), scale, inv);
+    const float inv_y = __fmul_rn(inv, kScale);
     const float scale_y = __fdiv_rn(scale, kScale);
     int8_t* qrow = p.q + static_cast<int64_t>(m) * p.ldq;
 #pragma unroll
@@ -609,7 +627,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
         float t[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          if constexpr (ROUNDING == 0)
+          if constexpr (ROUNDING != 1)
             t[j] = __fmul_rn(y[sl][16 * h + j], inv_y);
           else
             t[j] = __fdiv_rn(y[sl][16 * h + j], scale_y);

@@ -52,6 +52,9 @@ extern "C" {
                                   q = rint(y * (1/scale)) */
 #define CONVROT_ROUND_TORCH 1  /* reference torch path (int8.py:173-178), used there for M < 17 rows:
                                   exact dot rounded once to bf16, q = rint(y / scale) */
+#define CONVROT_ROUND_TRITON 2 /* as CONVROT_ROUND_KERNEL, with both divisions (scale = amax / 127, inv = 1 / scale)
+                                  done by PTX div.full.f32, the approximate division the reference's Triton
+                                  kernels run on the GPU: its B200 codes and scales */
 
 /*
  * Rotate + quantise (replaces int8.py:326-344).
