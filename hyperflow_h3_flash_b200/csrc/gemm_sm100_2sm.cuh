@@ -8,9 +8,10 @@
 //
 // Roles per CTA (224 threads; warp 6 only with the low-rank term):
 //   warp 0      TMA producer: this CTA's A tile and B half, signalling the LEADER's full barrier (cta_group::2 load)
-//   warp 1      TMEM allocation for the pair; in the leader (rank 0), lane 0 issues every MMA and commit
+//   warp 1      TMEM allocation for the pair; in the leader (rank 0), lane 0 issues the int8 main loop's MMAs
 //   warps 2..5  epilogue over this CTA's 128 accumulator rows (as in the 1-SM kernel)
-//   warp 6      TMA producer of this CTA's low-rank tiles (xa rows, up rows)
+//   warp 6      TMA producer of this CTA's low-rank tiles (xa rows, up rows); in the leader, lane 0 also issues the
+//               low-rank MMAs, so the main loop's issuer neither waits for nor polls anything of the low-rank term
 //
 // Cross-CTA signalling: TMA loads (never multicast: each CTA fetches its own bytes) complete on the leader's barrier
 // through its cluster address, the leader signals MMA completion to both CTAs' barriers with one tcgen05.commit,
@@ -149,9 +150,9 @@ struct Gemm2Cfg {
   static constexpr int kLRUpBytes = kHasLR ? kLRUpRows * LR_ATOM * LR_ATOMS : 0;
   static constexpr int kTmemCols = 512;
   static constexpr int kThreads = kHasLR ? 224 : 192;
-  // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2 x 2], lr_done[2 x 2], lr_full, lr_empty, drain
-  // (epi_ready and lr_done per accumulator buffer and 128-column half)
-  static constexpr int kNumBars = 2 * STAGES + 12 + 3;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2 x 2], lr_done[2 x 2], lr_full, lr_empty, drain,
+  // lr_drain (epi_ready and lr_done per accumulator buffer and 128-column half)
+  static constexpr int kNumBars = 2 * STAGES + 12 + 4;
   static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
   // Output staging: per epilogue warp two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B) for TMA stores.
   static constexpr int kStoreBoxBytes = 32 * 64;
@@ -193,6 +194,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* lr_full = tmem_full + 12;
   uint64_t* lr_empty = tmem_full + 13;
   uint64_t* drain = tmem_full + 14;
+  uint64_t* lr_drain = tmem_full + 15;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   uint16_t* silu_tab = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(bars) + Cfg::kBarBytes);
@@ -225,6 +227,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     mbar_init(lr_full, 1);
     mbar_init(lr_empty, 1);
     mbar_init(drain, 1);
+    mbar_init(lr_drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -289,74 +292,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (leader only)
+    // ------------------------------------------------------------ MMA issuer of the int8 main loop (leader only)
     if (lane == 0 && rank == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int pending_lr = -1;       // local tile index whose low-rank MMA is not issued yet
-      int pending_half = 0;      // its next 128-column half
-      int pending_chunk = 0;     // that half's next rank chunk
-      bool lr_epi_seen = false;  // both CTAs' epilogues have read that half's accumulator
-      uint32_t lr_full_phase = 0;
       const uint32_t ring_base = smem_u32(ring);
-      const uint32_t xa_base = smem_u32(lr_xa);
-      const uint32_t up_base = smem_u32(lr_up);
       const uint32_t empty_self = smem_u32(empty);
       const uint32_t tfull_self = smem_u32(tmem_full);
-      const uint32_t lrdone_self = smem_u32(lr_done);
-      const uint32_t lrempty_self = smem_u32(lr_empty);
-      // One rank chunk of the low-rank MMA of 128-column half h of local tile j (both CTAs' rows).  The half's
-      // first MMA overwrites its accumulator columns (the epilogue has read the int32 values and holds them
-      // dequantised in registers), so the product lands in TMEM on its own; the half's last chunk tells both CTAs'
-      // epilogues.
-      auto issue_lr_chunk = [&](int j, int h, int c, bool last) {
-        const uint32_t d = tmem_base + (j & 1) * BN + h * (BN / 2);
-        for (int a = 0; a < LR_ATOMS; ++a) {
-          for (int off = 0; off < LR_ATOM; off += 32) {
-            const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
-            const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kLRUpRows * LR_ATOM + off, LR_ATOM);
-            mma_f16_pair(d, ad, bd, Cfg::kIdescLR, (c | a | off) != 0);
-          }
-        }
-        if (last) mma_commit_pair_both(lrdone_self + ((j & 1) * 2 + h) * 8);
-        mma_commit_pair_both(lrempty_self);
-      };
-      auto lr_step = [&]() {
-        tc_fence_after();
-        const bool last = pending_chunk + 1 == lr_chunks;
-        issue_lr_chunk(pending_lr, pending_half, pending_chunk, last);
-        lr_full_phase ^= 1;
-        if (!last) {
-          ++pending_chunk;
-        } else if (pending_half == 0) {
-          pending_half = 1;
-          pending_chunk = 0;
-          lr_epi_seen = false;
-        } else {
-          pending_lr = -1;
-        }
-      };
-      auto lr_epi_bar = [&]() { return &epi_ready[(pending_lr & 1) * 2 + pending_half]; };
-      auto try_lr = [&]() {
-        if (!HAS_LR || pending_lr < 0) return;
-        if (!lr_epi_seen) {
-          if (!mbar_test_wait_cluster(lr_epi_bar(), (pending_lr >> 1) & 1)) return;
-          lr_epi_seen = true;
-        }
-        if (!mbar_test_wait(lr_full, lr_full_phase)) return;
-        lr_step();
-      };
-      auto flush_lr = [&]() -> bool {
-        while (HAS_LR && pending_lr >= 0) {
-          if (!lr_epi_seen) {
-            if (!mbar_wait_cluster_bounded(lr_epi_bar(), (pending_lr >> 1) & 1, limit, abort_flag)) return false;
-            lr_epi_seen = true;
-          }
-          if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
-          lr_step();
-        }
-        return true;
-      };
       int i = 0;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
         const uint32_t buf = i & 1;
@@ -367,17 +309,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (HAS_LR) {
-            const uint64_t t0 = globaltimer_ns();
-            for (uint32_t spin = 0; !mbar_try_wait(&full[stage], phase); ++spin) {
-              try_lr();
-              if ((spin & 63) == 63 && (*abort_flag || globaltimer_ns() - t0 > limit)) {
-                ok = false;
-                break;
-              }
-            }
-            if (!ok) break;
-          } else if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
+          if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
             ok = false;
             break;
           }
@@ -392,45 +324,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (HAS_LR) try_lr();
         }
         if (!ok) break;
         mma_commit_pair_both(tfull_self + buf * 8);
-        if (HAS_LR) {
-          if (!flush_lr()) {
-            ok = false;
-            break;
-          }
-          pending_lr = i;
-          pending_half = 0;
-          pending_chunk = 0;
-          lr_epi_seen = false;
-        }
       }
-      if (ok && !flush_lr()) ok = false;
       if (!ok) fail();
       mma_commit_pair(smem_u32(drain));
       volatile int never = 0;
       mbar_wait_bounded(drain, 0, limit, &never);
     }
   } else if (HAS_LR && warp == 6) {
-    // ------------------------------------------------------------ TMA producer: low-rank tiles of this CTA
+    // ------------------------------------------------------------ low-rank term: operand loads of this CTA, and in
+    // the leader also the kind::f16 MMAs, issued from this warp so that the main loop's issuer never waits or polls
+    // for them (each thread's tcgen05.commit tracks its own MMAs, and the two streams write different accumulator
+    // buffers).  Unit u = (local tile i, 128-column half h, rank chunk c).
     if (lane == 0) {
-      int u = 0;  // rank-chunk loads so far (all tiles, both halves)
+      int u = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
+      const uint32_t xa_base = smem_u32(lr_xa);
+      const uint32_t up_base = smem_u32(lr_up);
+      const uint32_t lrdone_self = smem_u32(lr_done);
+      const uint32_t lrempty_self = smem_u32(lr_empty);
+      int i = 0;
+      for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
-        // Per 128-column half h, this CTA holds up rows [128 h + 64 rank, + 64) of the tile (the pair's N = 128
-        // MMA splits its B operand between the two CTAs), and the xa rows of its 128 accumulator rows.
+        // Per half h, this CTA holds up rows [128 h + 64 rank, + 64) of the tile (the pair's N = 128 MMA splits its
+        // B operand between the two CTAs), and the xa rows of its 128 accumulator rows.
         for (int h = 0; ok && h < 2; ++h) {
           const int n0 = nb * BN + h * (BN / 2) + static_cast<int>(rank) * Cfg::kLRUpRows;
           for (int c = 0; c < lr_chunks; ++c, ++u) {
-            // load u reuses the operand buffers once the MMA of load u-1 (phase u-1 of lr_empty) is done
+            // unit u reuses the operand buffers once the MMAs of unit u-1 (phase u-1 of lr_empty) are done
             if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
-              fail();
               ok = false;
               break;
             }
@@ -440,12 +367,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
               tma_load_2d_pair(lr_xa + a * kBM * LR_ATOM, &tmap_xa, leader_lr_full, x + xs, m0);
               tma_load_2d_pair(lr_up + a * Cfg::kLRUpRows * LR_ATOM, &tmap_up, leader_lr_full, x, n0);
             }
+            if (rank != 0) continue;
+            // both CTAs' operands have landed, and (first chunk) both epilogues have read the half's accumulator
+            if (!mbar_wait_bounded(lr_full, u & 1, limit, abort_flag) ||
+                (c == 0 && !mbar_wait_cluster_bounded(&epi_ready[(i & 1) * 2 + h], (i >> 1) & 1, limit, abort_flag))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // The half's first MMA overwrites its accumulator columns (the epilogue holds the dequantised values in
+            // registers), so the product lands in TMEM on its own; the half's last chunk tells both epilogues.
+            const uint32_t d = tmem_base + (i & 1) * BN + h * (BN / 2);
+            for (int a = 0; a < LR_ATOMS; ++a) {
+              for (int off = 0; off < LR_ATOM; off += 32) {
+                const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
+                const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kLRUpRows * LR_ATOM + off, LR_ATOM);
+                mma_f16_pair(d, ad, bd, Cfg::kIdescLR, (c | a | off) != 0);
+              }
+            }
+            if (c + 1 == lr_chunks) mma_commit_pair_both(lrdone_self + ((i & 1) * 2 + h) * 8);
+            mma_commit_pair_both(lrempty_self);
           }
         }
       }
       if (!ok) {
-        const uint64_t t0 = globaltimer_ns();
+        fail();
+        const uint64_t t0 = globaltimer_ns();  // let loads in flight land (their barrier may be the peer's)
         while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+      }
+      if (rank == 0) {  // this thread's MMAs are done before the CTA may free its TMEM
+        mma_commit_pair(smem_u32(lr_drain));
+        volatile int never = 0;
+        mbar_wait_bounded(lr_drain, 0, limit, &never);
       }
     }
   } else if (warp >= 2 && warp <= 5) {
