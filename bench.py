@@ -53,9 +53,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "rotate_ffn_down",
-                                       "down"],
+                                       "down", "step"],
                     default=None,
-                    help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches")
+                    help="run one kernel alone (for ncu captures): --rows rows, K=N=5120, 3 warm-up + 3 launches; "
+                         "'step': --warmup + --steps steps of the config-2 linear set and nothing else (launch lists)")
     return ap.parse_args()
 
 
@@ -1034,6 +1035,30 @@ def run_case(args) -> None:
 
     dev = torch.device("cuda", 0)
     M = args.rows
+    if args.case == "step":  # the bench's step alone (1 GPU): its kernels' launch list, no extras or baselines
+        from hyperflow_h3_flash_b200 import ulysses
+
+        layers = []
+        for i in range(4):
+            w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP, seed_offset=i)
+            layer = I.Int8RotLinear(K_DIM, N_DIM, GROUP, bias=True, rank=RANK)
+            synthetic.load_into(layer, w)
+            layers.append(layer.to(dev))
+        layers[0].keep_input = layers[1].keep_input = True
+        I.share_lowrank(*layers[:3])
+        x = synthetic.activations(M, K_DIM).to(dev)
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.inference_mode():
+            for i in range(args.warmup + args.steps):
+                if i == args.warmup:
+                    torch.cuda.synchronize()
+                    st.record()
+                ulysses.attention_block_linears(x, *layers, HEADS)
+            en.record()
+            en.synchronize()
+        print(json.dumps({"case": "step", "rows": M, "ms_per_step": st.elapsed_time(en) / max(args.steps, 1)}),
+              flush=True)
+        return
     x = synthetic.activations(M, K_DIM).to(dev)
     w = synthetic.linear_weights(K_DIM, N_DIM, rank=RANK, bias=True, group=GROUP).to(dev)
     q, s = I.rotate_quant(x, GROUP)
