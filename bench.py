@@ -52,6 +52,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="Ulysses exchange for N > 1: fused into the kernels over peer memory, or NCCL all-to-all")
+    ap.add_argument("--peer-copies", default="",
+                    help="peer transport: projections (of q, k, v) written locally and moved by the copy engines "
+                         "while the next GEMM runs; the others store into the other GPUs' buffers from the epilogue")
     ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "rotate_ffn_down",
                                        "down", "step"],
                     default=None,
@@ -264,13 +267,16 @@ METRIC_DETAIL = ("value: INT8 TOPS of the config-2 linear set (the config-2 conv
 DATA = "synthetic (seeded, random-init weights)"
 
 
-def workload_config(rows: int, world: int, transport: str) -> dict:
+def workload_config(rows: int, world: int, transport: str, peer_copies: str = "") -> dict:
     """The `config` object of both arms' lines (the reference arm times a row sample of this same workload)."""
     exchange = world > 1 and transport == "peer"
     return {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
                         f"M={rows} rows/rank, K=N={K_DIM}, r={RANK}, bias, group {GROUP}"
                         + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity attention"
-                           + (" (fused into the kernels over peer memory)" if exchange else " (NCCL)")
+                           + ((" (over peer memory: " + (", ".join(peer_copies) + " written locally and moved by the "
+                                                          "copy engines, " if peer_copies else "")
+                               + "the rest stored by the GEMM epilogue; gathered by the out projection's rotate "
+                                 "kernel)") if exchange else " (NCCL)")
                            if world > 1 else ""),
             "rows_per_rank": rows, "total_rows": rows * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
             "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
@@ -288,7 +294,7 @@ def run_reference(args) -> None:
         "unit": "TOPS", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": DATA, "impl": "reference",
-        "config": workload_config(args.rows, args.gpus, args.transport),
+        "config": workload_config(args.rows, args.gpus, args.transport, args.peer_copies),
         "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": res["value"], "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -452,7 +458,7 @@ def run_ours(args) -> None:
     if world > 1 and args.transport == "peer":
         # every rank must agree on the transport: a rank whose mapping fails tells the others through an all-reduce
         try:
-            exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev)
+            exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies))
             failed = 0
         except Exception as e:  # noqa: BLE001 - reported, and the NCCL transport is used instead
             print(f"peer-memory exchange unavailable on rank {rank}: {e}; using NCCL all-to-all", file=sys.stderr)
@@ -574,7 +580,7 @@ def run_ours(args) -> None:
             "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": DATA,
-            "config": workload_config(M, world, args.transport),
+            "config": workload_config(M, world, args.transport, args.peer_copies),
             "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2,
                     "pipelining": "H2D / compute / D2H on three streams, double-buffered"},
@@ -638,7 +644,7 @@ def strong_scaling_cfg4(torch, dist, synthetic, ulysses, dev, rank, world, args,
     xs = synthetic.activations(rows, K_DIM, seed=100 + rank).to(dev)
     exchange = None
     if world > 1 and args.transport == "peer":
-        exchange = ulysses.PeerExchange(rows, N_DIM, HEADS, device=dev)
+        exchange = ulysses.PeerExchange(rows, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies))
 
     def step():
         return ulysses.attention_block_linears(xs, to_q, to_k, to_v, to_out, HEADS, exchange=exchange)

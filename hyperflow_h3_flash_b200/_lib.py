@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "convrot_ipc_close": ([_P], _I),
     "convrot_peer_signal": ([_P, _I, _U32, _P], _I),
     "convrot_peer_wait": ([_P, _I, _U32, _P], _I),
+    "convrot_copy_blocks": ([_P, _P, _P, _I, _P], _I),
     "convrot_workspace_size": ([_L, _L, _L], _S),
     "convrot_linear": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _S, _P, _L, _P], _I),
     "convrot_linear_noalloc": ([_P, _L, _P, _L, _P, _P, _P, _L, _P, _L, _L, _L, _L, _L, _I, _P, _L, _P], _I),

@@ -918,6 +918,23 @@ int convrot_peer_wait(const uint32_t* flags, int n, uint32_t epoch, void* stream
   return e == cudaSuccess ? CONVROT_OK : cuda_fail(e);
 }
 
+int convrot_copy_blocks(void* const* dst, const void* const* src, const size_t* bytes, int n, void* stream) {
+  if (n < 0 || n > 64 || (n > 0 && (!dst || !src || !bytes))) return CONVROT_ERR_ARG;
+  for (int j = 0; j < n; ++j)
+    if ((!dst[j] || !src[j]) && bytes[j]) return CONVROT_ERR_ARG;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  // One plain cudaMemcpyAsync per block (copy engines; no batched-copy API).
+  for (int j = 0; j < n; ++j) {
+    if (!bytes[j]) continue;
+    const cudaError_t e = cudaMemcpyAsync(dst[j], src[j], bytes[j], cudaMemcpyDeviceToDevice,
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e);
+  }
+  return CONVROT_OK;
+}
+
 int convrot_lowrank_down(const void* x, int64_t ldx, const void* lr_down, int64_t ld_down, int64_t M, int64_t K,
                          int64_t r, void* xa_out, int64_t ldxa, void* stream) {
   return lowrank_down(x, ldx, lr_down, ld_down, M, K, r, xa_out, ldxa, static_cast<cudaStream_t>(stream));

@@ -72,8 +72,12 @@ class PeerExchange:
     The buffers live in this GPU's memory; every other rank maps them through CUDA IPC (one process per GPU), so
     the q/k/v GEMMs of rank i store column block j of their outputs straight into rank j's receive buffer, slot i
     (``convrot_gemm_scatter``), and the out projection's rotate kernel of rank i reads block i of every rank's
-    attention output straight from that rank's memory (``convrot_rotate_quant_gather``).  No copy, no collective
-    library: the bytes cross NVLink inside the kernels that produce and consume them.
+    attention output straight from that rank's memory (``convrot_rotate_quant_gather``): the bytes cross NVLink
+    inside the kernels that produce and consume them.  Layers named in ``copy_names`` instead write their output
+    locally in the send layout and the GPU's copy engines move the blocks into the other ranks' buffers on a stream
+    of their own, overlapping the next GEMM (``convrot_copy_blocks``).  Measured on 2 B200s that is slower (3.44
+    against 3.15 ms per config-2 step with q and k copied: the copies contend with the next GEMM for HBM and
+    NVLink), so the default is none.  No collective library either way.
 
     Ordering is two epoch flags per step (``convrot_peer_signal`` / ``convrot_peer_wait``, release/acquire at
     system scope, bounded waits):
@@ -93,7 +97,8 @@ class PeerExchange:
     _NAMES = ("q", "k", "v", "out")
     _FLAG_BYTES = 4096
 
-    def __init__(self, rows: int, width: int, heads: int, group=None, device: torch.device | None = None):
+    def __init__(self, rows: int, width: int, heads: int, group=None, device: torch.device | None = None,
+                 copy_names: tuple[str, ...] = ()):
         from . import _lib
 
         self._lib = _lib
@@ -139,6 +144,13 @@ class PeerExchange:
             raise RuntimeError(error or "another rank could not map the exchange buffers")
         self.epoch = 0
         self.kernel_launches = 0
+        # Layers (of "q", "k", "v") whose output is written locally in the send layout and then moved into the
+        # other GPUs' receive buffers by the copy engines, on their own stream, while the next GEMM runs; the rest
+        # store straight into the other GPUs' buffers from the GEMM epilogue.
+        if any(n not in ("q", "k", "v") for n in copy_names):
+            raise ValueError(f"copy_names must name q, k or v, got {copy_names!r}")
+        self.copy_names = tuple(copy_names)
+        self.copy_stream = torch.cuda.Stream(self.device)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
 
@@ -158,6 +170,22 @@ class PeerExchange:
 
     def step(self) -> None:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+
+    def copy_out(self, name: str, packed: Tensor) -> None:
+        """Moves ``packed`` (``[P, rows, W]``, block j for rank j) into every rank's receive buffer ``name`` at this
+        rank's slot, on the copy stream, after the work queued so far on the current stream (the GEMM that wrote it).
+        ``join_copies`` makes the current stream wait for these copies."""
+        compute = torch.cuda.current_stream(self.device)
+        self.copy_stream.wait_stream(compute)
+        dst = (ctypes.c_void_p * self.P)(*self.block_ptrs(name))
+        src = (ctypes.c_void_p * self.P)(*[packed[j].data_ptr() for j in range(self.P)])
+        nbytes = (ctypes.c_size_t * self.P)(*([self.rows * self.W * 2] * self.P))
+        stream = ctypes.c_void_p(self.copy_stream.cuda_stream)
+        self._lib.check(self._lib.lib().convrot_copy_blocks(dst, src, nbytes, self.P, stream), "convrot_copy_blocks")
+        packed.record_stream(self.copy_stream)  # not recycled by the allocator before the copies have read it
+
+    def join_copies(self) -> None:
+        torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
 
     def signal(self, phase: int) -> None:
         slots = (ctypes.c_void_p * self.P)(*[b + 4 * (8 * phase + self.rank) for b in self.base])
@@ -196,7 +224,12 @@ def attention_block_peer(x: Tensor, to_q, to_k, to_v, to_out, exchange: PeerExch
     P, d = ex.P, ex.width // ex.heads
     ex.step()
     for name, layer in zip("qkv", (to_q, to_k, to_v)):
-        layer.forward_scatter(x, ex.block_ptrs(name), ex.W)
+        if name in ex.copy_names:
+            ex.copy_out(name, layer(x, out_chunks=P))  # local send layout, then the copy engines
+        else:
+            layer.forward_scatter(x, ex.block_ptrs(name), ex.W)
+    if ex.copy_names:
+        ex.join_copies()
     ex.signal(ex.ARRIVED)
     ex.wait(ex.ARRIVED)
     if attention is None:

@@ -220,6 +220,14 @@ int convrot_peer_signal(uint32_t* const* slots, int n, uint32_t epoch, void* str
 int convrot_peer_wait(const uint32_t* flags, int n, uint32_t epoch, void* stream);
 
 /*
+ * n device-to-device block copies on `stream`, dst[j] <- src[j] (bytes[j] each, 0 skips), one cudaMemcpyAsync per
+ * block so that the GPU's copy engines move them (no counterpart in the reference: exchange plumbing).  Used by the
+ * peer exchange for layers whose output is written locally and then copied into the other GPUs' receive buffers
+ * while the next GEMM runs on the SMs.  At most 64 blocks.
+ */
+int convrot_copy_blocks(void* const* dst, const void* const* src, const size_t* bytes, int n, void* stream);
+
+/*
  * Workspace for convrot_linear: q (int8 [M, K] with rows padded to a multiple of 16 bytes), s (fp32 [M]) and xa
  * (bf16 [M, r] with rows padded to a multiple of 8 elements), each 256-byte aligned.  Exactly the size
  * convrot_linear requires; 0 for negative arguments.
