@@ -977,18 +977,34 @@ def run_extras(torch, I, synthetic, dev, args, x) -> dict:
     from hyperflow_h3_flash_b200.grouped import GroupedInt8RotLinear
 
     kv_group = GroupedInt8RotLinear(*kv_layers)
+    # the reference's own modules on the same weights (its Triton and cuBLASLt kernels, eager as it runs)
+    ref, _ = load_reference_int8()
+    ref_kv = None
+    if ref is not None and ref._kernels() is not None:
+        ref.set_kernel_options(rotate_quant="factored", int8_gemm="auto")
+        ref_parts = reference_layers(ref, torch, dev, 4096, K_DIM, RANK, 2, seed0=80)
+
+        def ref_kv(t):
+            ref_parts[0][0].keep_input = True
+            return reference_linear(t, ref_parts[0]), reference_linear(t, ref_parts[1])
+
     cfg5 = {}
     for rows in (256, 333):
         xt = synthetic.activations(rows, 4096, seed=rows).to(dev)
         graphed = CapturedCall(kv, xt)
         graphed_group = CapturedCall(kv_group, xt)
-        t = timed_ab({"eager": lambda: kv(xt), "graph": lambda: graphed(xt),
-                      "grouped_graph": lambda: graphed_group(xt)}, args.steps * 5)
-        cfg5[f"M{rows}"] = {"eager_us": t["eager"] * 1e3, "graph_us": t["graph"] * 1e3,
-                            "grouped_graph_us": t["grouped_graph"] * 1e3}
+        variants = {"eager": lambda: kv(xt), "graph": lambda: graphed(xt), "grouped_graph": lambda: graphed_group(xt)}
+        if ref_kv is not None:
+            variants["reference_eager"] = lambda: ref_kv(xt)
+        t = timed_ab(variants, args.steps * 5)
+        cfg5[f"M{rows}"] = {f"{k}_us": v * 1e3 for k, v in t.items()}
+    if ref is not None:
+        ref.Int8RotLinear._last_input.clear()
     out["cross_attention_kv_cfg5"] = {"config": "config 5: K and V projections 4096 -> 5120 (r=32, bias, shared "
                                                 "quantisation) on 256 / 333 text tokens, per call; grouped = one "
-                                                "quantisation, one down projection and one GEMM launch for both",
+                                                "quantisation, one down projection and one GEMM launch for both; "
+                                                "reference_eager = the reference's own Int8RotLinear (Triton "
+                                                "factored rotate, cuBLASLt + rescale) + bias + LowRankLinear",
                                       **cfg5}
 
     # config 2's q / k / v as three layers (shared quantisation and down projection) or as one grouped launch

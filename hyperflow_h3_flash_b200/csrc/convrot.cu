@@ -365,8 +365,8 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   if (has_lr) {
     if ((rc = make_map(&txa, xa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, r * lr_segments, ldxa, kBM, lr_atom / 2)))
       return rc;
-    // up rows per load: the 1-SM tile's 256, or the 2-SM CTA's 64-row share of one 128-column half
-    const int up_rows = two_sm ? 64 : b_rows;
+    // up rows per load: one 128-column half of the tile (1-SM), or the 2-SM CTA's 64-row share of one half
+    const int up_rows = two_sm ? 64 : 128;
     if ((rc = make_map(&tup, up, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, r, ld_up, up_rows, lr_atom / 2))) return rc;
   }
   GemmParams p;

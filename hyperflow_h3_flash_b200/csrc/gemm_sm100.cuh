@@ -103,17 +103,20 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * kRowBytes;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kLRXaBytes = kHasLR ? kBM * LR_ATOM * LR_ATOMS : 0;
-  static constexpr int kLRUpBytes = kHasLR ? BN * LR_ATOM * LR_ATOMS : 0;
+  // The low-rank term runs per half of the tile's columns: one half's up rows at a time.
+  static constexpr int kLRUpRows = BN / 2;
+  static constexpr int kLRUpBytes = kHasLR ? kLRUpRows * LR_ATOM * LR_ATOMS : 0;
   static constexpr int kMmaPerStage = 4;  // 32 bytes of K per MMA
   static constexpr int kTmemCols = tmem_cols_for(BN);
   static constexpr int kThreads = kHasLR ? 224 : 192;
-  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2], lr_done[2], lr_full, lr_empty, drain
-  static constexpr int kNumBars = 2 * STAGES + 8 + 3;
+  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], epi_ready[2 x 2], lr_done[2 x 2], lr_full, lr_empty,
+  // drain, lr_drain (epi_ready and lr_done per accumulator buffer and half of the columns)
+  static constexpr int kNumBars = 2 * STAGES + 12 + 4;
   static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
   static constexpr int kSmemBytes = 1024 /*alignment slack*/ + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes +
                                     kBarBytes;
   static constexpr uint32_t kIdesc = KIND == KIND_I8 ? make_idesc_i8(kBM, BN) : make_idesc_bf16(kBM, BN);
-  static constexpr uint32_t kIdescLR = make_idesc_bf16(kBM, BN);
+  static constexpr uint32_t kIdescLR = make_idesc_bf16(kBM, BN / 2);  // one half of the columns per low-rank MMA
 };
 
 __device__ __forceinline__ void record_error(int* word, int code) {
@@ -333,11 +336,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* empty = bars + S;
   uint64_t* tmem_full = bars + 2 * S;
   uint64_t* tmem_empty = tmem_full + 2;
-  uint64_t* epi_ready = tmem_full + 4;
-  uint64_t* lr_done = tmem_full + 6;
-  uint64_t* lr_full = tmem_full + 8;
-  uint64_t* lr_empty = tmem_full + 9;
-  uint64_t* drain = tmem_full + 10;
+  uint64_t* epi_ready = tmem_full + 4;  // [buf * 2 + half]
+  uint64_t* lr_done = tmem_full + 8;    // [buf * 2 + half]
+  uint64_t* lr_full = tmem_full + 12;
+  uint64_t* lr_empty = tmem_full + 13;
+  uint64_t* drain = tmem_full + 14;
+  uint64_t* lr_drain = tmem_full + 15;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -368,12 +372,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
       mbar_init(&tmem_empty[b], 4);
+    }
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&epi_ready[b], 4);
       mbar_init(&lr_done[b], 1);
     }
     mbar_init(lr_full, 1);
     mbar_init(lr_empty, 1);
     mbar_init(drain, 1);
+    mbar_init(lr_drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -443,59 +450,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int pending_lr = -1;  // local tile index whose low-rank MMA is not issued yet
-      int pending_chunk = 0;  // its next rank chunk
-      bool lr_epi_seen = false;  // its epilogue pass 1 is done
-      uint32_t lr_full_phase = 0;
       const uint32_t ring_base = smem_u32(ring);
-      const uint32_t xa_base = smem_u32(lr_xa);
-      const uint32_t up_base = smem_u32(lr_up);
-      // Issues one rank chunk of the low-rank MMA of local tile j: D[buf j] += xa_chunk . up_chunk^T (kind::f16,
-      // K = 16 per MMA); the last chunk also signals the epilogue.
-      auto issue_lr_chunk = [&](int j, bool last) {
-        const uint32_t d = tmem_base + (j & 1) * BN;
-        for (int a = 0; a < LR_ATOMS; ++a) {
-          for (int off = 0; off < LR_ATOM; off += 32) {
-            const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
-            const uint64_t bd = make_kmajor_desc(up_base + a * BN * LR_ATOM + off, LR_ATOM);
-            mma_f16(d, ad, bd, Cfg::kIdescLR, 1u);
-          }
-        }
-        if (last) mma_commit(&lr_done[j & 1]);
-        mma_commit(lr_empty);
-      };
-      auto lr_step = [&]() {
-        tc_fence_after();
-        const bool last = pending_chunk + 1 == lr_chunks;
-        issue_lr_chunk(pending_lr, last);
-        lr_full_phase ^= 1;
-        if (last)
-          pending_lr = -1;
-        else
-          ++pending_chunk;
-      };
-      // Non-blocking: issue the pending tile's next rank chunk once its epilogue pass 1 and the chunk are in place.
-      auto try_lr = [&]() {
-        if (!HAS_LR || pending_lr < 0) return;
-        if (!lr_epi_seen) {
-          if (!mbar_test_wait(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1)) return;
-          lr_epi_seen = true;
-        }
-        if (!mbar_test_wait(lr_full, lr_full_phase)) return;
-        lr_step();
-      };
-      auto flush_lr = [&]() -> bool {
-        while (HAS_LR && pending_lr >= 0) {
-          if (!lr_epi_seen) {
-            if (!mbar_wait_bounded(&epi_ready[pending_lr & 1], (pending_lr >> 1) & 1, limit, abort_flag))
-              return false;
-            lr_epi_seen = true;
-          }
-          if (!mbar_wait_bounded(lr_full, lr_full_phase, limit, abort_flag)) return false;
-          lr_step();
-        }
-        return true;
-      };
       int i = 0;
       for (int tile = tile0; ok && tile < num_tiles; tile += tile_step, ++i) {
         const uint32_t buf = i & 1;
@@ -506,18 +461,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
-          // wait for the stage, issuing a pending low-rank MMA while the data is in flight
-          if (HAS_LR) {
-            const uint64_t t0 = globaltimer_ns();
-            for (uint32_t spin = 0; !mbar_try_wait(&full[stage], phase); ++spin) {
-              try_lr();
-              if ((spin & 63) == 63 && (*abort_flag || globaltimer_ns() - t0 > limit)) {
-                ok = false;
-                break;
-              }
-            }
-            if (!ok) break;
-          } else if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
+          if (!mbar_wait_bounded(&full[stage], phase, limit, abort_flag)) {
             ok = false;
             break;
           }
@@ -539,21 +483,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (HAS_LR) try_lr();
         }
         if (!ok) break;
         mma_commit(&tmem_full[buf]);
-        if (HAS_LR) {
-          if (!flush_lr()) {  // the previous tile's low-rank MMA must go before this one's
-            ok = false;
-            break;
-          }
-          pending_lr = i;
-          pending_chunk = 0;
-          lr_epi_seen = false;
-        }
       }
-      if (ok && !flush_lr()) ok = false;
       if (!ok) fail();
       // Make sure no MMA is still reading shared memory or writing TMEM when the CTA winds down.
       mma_commit(drain);
@@ -561,39 +494,66 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       mbar_wait_bounded(drain, 0, limit, &never);
     }
   } else if (HAS_LR && warp == 6) {
-    // ---------------------------------------------------------------- TMA producer (low-rank operand tiles)
+    // ---------------------------------------------------------------- low-rank term: operand loads and MMAs
+    // Issued from this warp so that the main loop's issuer never waits or polls for them (each thread's
+    // tcgen05.commit tracks its own MMAs, and the two streams write different accumulator buffers).  Unit u =
+    // (local tile i, half h of the columns, rank chunk c).
     if (lane == 0) {
-      bool loaded = false;
-      uint32_t loaded_parity = 0;
-      int u = 0;  // rank chunks loaded so far (all tiles)
+      int u = 0;
       bool ok = true;
-      for (int tile = tile0; ok && tile < num_tiles; tile += tile_step) {
+      const uint32_t xa_base = smem_u32(lr_xa);
+      const uint32_t up_base = smem_u32(lr_up);
+      int i = 0;
+      for (int tile = tile0; ok && tile < num_tiles; tile += tile_step, ++i) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * kBM;
-        const int n0 = nb * BN;
-        for (int c = 0; c < lr_chunks; ++c, ++u) {
-          // load u reuses the operand buffer once the MMA of load u-1 (phase u-1 of lr_empty) is done
-          if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
-            fail();
-            ok = false;
-            break;
+        const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
+        for (int h = 0; ok && h < 2; ++h) {
+          const int n0 = nb * BN + h * Cfg::kLRUpRows;
+          for (int c = 0; c < lr_chunks; ++c, ++u) {
+            // unit u reuses the operand buffers once the MMAs of unit u-1 (phase u-1 of lr_empty) are done
+            if (!mbar_wait_bounded(lr_empty, (u & 1) ^ 1, limit, abort_flag)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
+            for (int a = 0; a < LR_ATOMS; ++a) {
+              const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
+              tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, x + xs, m0);
+              tma_load_2d(lr_up + a * Cfg::kLRUpRows * LR_ATOM, &tmap_up, lr_full, x, n0);
+            }
+            // the operands have landed, and (first chunk) the epilogue has read the half's accumulator
+            if (!mbar_wait_bounded(lr_full, u & 1, limit, abort_flag) ||
+                (c == 0 && !mbar_wait_bounded(&epi_ready[(i & 1) * 2 + h], (i >> 1) & 1, limit, abort_flag))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // The half's first MMA overwrites its accumulator columns (the epilogue holds the dequantised values in
+            // registers); the half's last chunk tells the epilogue.
+            const uint32_t d = tmem_base + (i & 1) * BN + h * Cfg::kLRUpRows;
+            for (int a = 0; a < LR_ATOMS; ++a) {
+              for (int off = 0; off < LR_ATOM; off += 32) {
+                const uint64_t ad = make_kmajor_desc(xa_base + a * kBM * LR_ATOM + off, LR_ATOM);
+                const uint64_t bd = make_kmajor_desc(up_base + a * Cfg::kLRUpRows * LR_ATOM + off, LR_ATOM);
+                mma_f16(d, ad, bd, Cfg::kIdescLR, (c | a | off) != 0);
+              }
+            }
+            if (c + 1 == lr_chunks) mma_commit(&lr_done[(i & 1) * 2 + h]);
+            mma_commit(lr_empty);
           }
-          mbar_arrive_expect_tx(lr_full, Cfg::kLRXaBytes + Cfg::kLRUpBytes);
-          const int xs = p.lr_seg_n ? (n0 / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
-          for (int a = 0; a < LR_ATOMS; ++a) {
-            const int x = (c * LR_ATOMS + a) * (LR_ATOM / 2);
-            tma_load_2d(lr_xa + a * kBM * LR_ATOM, &tmap_xa, lr_full, x + xs, m0);
-            tma_load_2d(lr_up + a * BN * LR_ATOM, &tmap_up, lr_full, x, n0);
-          }
-          loaded = true;
-          loaded_parity = u & 1;
         }
       }
-      if (loaded && *abort_flag) {
+      if (!ok) {
+        fail();
+        // a load still in flight lands before the CTA leaves (bounded)
         volatile int never = 0;
-        mbar_wait_bounded(lr_full, loaded_parity, limit, &never);
+        if (u > 0) mbar_wait_bounded(lr_full, (u - 1) & 1, limit, &never);
       }
+      mma_commit(lr_drain);  // this thread's MMAs are done before the CTA may free its TMEM
+      volatile int never = 0;
+      mbar_wait_bounded(lr_drain, 0, limit, &never);
     }
   } else if (warp >= 2 && warp <= 5) {
     // ---------------------------------------------------------------- epilogue
@@ -616,7 +576,59 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const bool row_ok = row < p.M;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
 
-      if (EPI == EPI_DEQUANT) {
+      if (EPI == EPI_DEQUANT && HAS_LR) {
+        // Per half of the columns: read the int32 accumulators and hold the dequantised values (+ bias) in
+        // registers, tell the low-rank warp that the half's columns are free, and wait while its MMA writes
+        // xa . up^T over them (accumulate = 0); then y = held + product, rounded once to bf16 on the way out.
+        const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
+        const int n_out = p.swiglu ? p.N >> 1 : p.N;
+        uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
+        bool lr_ok = true;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          float hold[BN / 2];
+#pragma unroll
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int c = h * (BN / 2) + cc * 32;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            float t[32];
+            dequant_chunk(v, sa, p.sb, p.bias, n0 + c, p.N, t);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) hold[cc * 32 + j] = t[j];
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&epi_ready[buf * 2 + h]);
+          if (!mbar_wait_bounded(&lr_done[buf * 2 + h], par, limit, abort_flag)) {
+            lr_ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int cc = 0; cc < BN / 64; ++cc) {
+            const int c = h * (BN / 2) + cc * 32;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(taddr + c, v);
+            tmem_ld_wait();
+            if (!row_ok) continue;
+            float t[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) t[j] = __fadd_rn(hold[cc * 32 + j], __uint_as_float(v[j]));
+            if (!p.swiglu) {
+              if (p.res) gated_residual(t, p, row, n0 + c);
+              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
+            } else if (swiglu_block(t, c, ya, nullptr)) {
+              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n0 + c - 32) >> 1), t, (n0 + c - 32) >> 1, n_out);
+            }
+          }
+        }
+        if (!lr_ok) {
+          fail();
+          break;
+        }
+      } else if (EPI == EPI_DEQUANT) {
         const float sa = row_ok ? __ldg(p.sa + row) : 0.0f;
         const int n_out = p.swiglu ? p.N >> 1 : p.N;
         uint32_t ya[16];  // SwiGLU: the bf16 `a` block awaiting its `g` block
@@ -628,45 +640,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const int n = n0 + c;
           float t[32];
           dequant_chunk(v, sa, p.sb, p.bias, n, p.N, t);
-          if (HAS_LR) {
-            uint32_t w[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(t[j]);
-            tmem_st_32x32b_x32(taddr + c, w);
-          } else if (!p.swiglu) {
+          if (!p.swiglu) {
             if (row_ok) {
               if (p.res) gated_residual(t, p, row, n);
               store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n), t, n, p.N);
             }
           } else if (swiglu_block(t, c, ya, nullptr) && row_ok) {
             store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n - 32) >> 1), t, (n - 32) >> 1, n_out);
-          }
-        }
-        if (HAS_LR) {
-          // pass 2: the low-rank MMA adds xa . up^T onto the fp32 values written above
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&epi_ready[buf]);
-          if (!mbar_wait_bounded(&lr_done[buf], par, limit, abort_flag)) {
-            fail();
-            break;
-          }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 32) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(taddr + c, v);
-            tmem_ld_wait();
-            if (!row_ok) continue;
-            float t[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) t[j] = __uint_as_float(v[j]);
-            if (!p.swiglu) {
-              if (p.res) gated_residual(t, p, row, n0 + c);
-              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, n0 + c), t, n0 + c, p.N);
-            } else if (swiglu_block(t, c, ya, nullptr))
-              store_bf16_chunk(out_ptr<__nv_bfloat16>(p, row, (n0 + c - 32) >> 1), t, (n0 + c - 32) >> 1, n_out);
           }
         }
       } else if (EPI == EPI_RAW_I32) {
