@@ -302,9 +302,9 @@ def test_one_and_two_sm_kernels_agree_bitwise(M, N, K, r):
         finally:
             _lib.lib().convrot_set_gemm_mode(0)
     assert torch.equal(outs[0][1], outs[1][1])
-    # the low-rank MMA accumulates 256 vs 128 rows per instruction: allow the fp32 accumulation order to differ
-    a, b = outs[0][0].float(), outs[1][0].float()
-    assert ((a - b).abs() <= a.abs() * 2.0**-7 + 1e-2 * a.abs().max()).all()
+    # both kernels hold the dequantised values and add a separately computed low-rank product (its MMA over the
+    # same K steps, 128 or 256 rows per instruction): the fused outputs are bitwise equal as well
+    assert torch.equal(outs[0][0], outs[1][0])
 
 
 def test_shared_lowrank_projection_matches_separate_layers(monkeypatch):
