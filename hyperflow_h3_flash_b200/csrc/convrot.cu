@@ -538,9 +538,9 @@ int launch_rq(const DeviceState& st, const RotQuantParams& p, cudaStream_t strea
 // G = 256: the two-column team kernel (8 threads per group).
 int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t stream) {
   const int ngroups = p.K / 256;
-  int slots = 1;
-  while ((ngroups * 8 + slots - 1) / slots > 512) slots *= 2;
-  if (slots > 2) return CONVROT_ERR_SHAPE;
+  // One group per thread up to 256 threads (K = 8192), two groups per thread beyond (up to 512 threads)
+  const int slots = ngroups * 8 <= 256 ? 1 : 2;
+  if ((ngroups * 8 + slots - 1) / slots > 512) return CONVROT_ERR_SHAPE;
   int threads = (ngroups * 8 + slots - 1) / slots;
   threads = (threads + 31) / 32 * 32;
   RotQuantParams q = p;
@@ -656,9 +656,9 @@ int rotate_quant(const void* x, int64_t ldx, int64_t M, int64_t K, int group, in
     case 16: return launch_rq<16>(*st, p, stream);
     case 64: return launch_rq<64>(*st, p, stream);
     default: {
-      // The two-column kernel while a row needs at most 256 threads (K <= 8192); beyond, the one-column kernel
-      // keeps more rows resident per SM (measured: K = 13824 -> 0.58 ms vs 0.80 ms).
-      const bool two_col = g_rq_variant == 0 && (K / 256) * 8 <= 256;
+      // The two-column kernel up to K = 16384 (two groups per thread above K = 8192: at K = 13824 0.545 ms against
+      // 0.568 ms for the one-column kernel, and 0.80 ms for one group per thread); the one-column kernel beyond.
+      const bool two_col = g_rq_variant == 0 && (K / 256) * 8 <= 512;
       if (g_rq_variant == 2) return launch_rq256(*st, p, stream);
       return two_col ? launch_rq256(*st, p, stream) : launch_rq<256>(*st, p, stream);
     }
