@@ -366,7 +366,7 @@ __host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stage
   const size_t tr = static_cast<size_t>(threads / 8) * 8 * kTrRow * 8;  // per team: 8 rows of the half transpose
   const size_t table = chunked ? static_cast<size_t>(K / 256) * sizeof(RQ256Piece) : 0;
   const size_t stats = 64 * 8;  // AdaLN: per-warp (sum, sum of squares) in fp64
-  return static_cast<size_t>(stages) * slots + tr + 32 * 4 + kRQMaxStages * 8 + stats + table + 64;
+  return static_cast<size_t>(stages) * slots + tr + 64 * 4 + kRQMaxStages * 8 + stats + table + 64;
 }
 
 // AdaLN on a pair of bf16 values (low half = even column): n = bf16((x - mean) * rstd) in fp32, then
@@ -411,8 +411,9 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
   const size_t stage_bytes = static_cast<size_t>(ngroups) * kSlotBytes;
   uint8_t* rows = rq2_smem_raw;
   double* tr = reinterpret_cast<double*>(rq2_smem_raw + stages * stage_bytes);
+  // per-warp row maxima, two sets used by alternate rows (so plain rows need one block barrier per row)
   float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr / 8) * 8 * kTrRow);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 64);
   double* stats = reinterpret_cast<double*>(bars + kRQMaxStages);  // ADALN: (sum, sum of squares) per warp
   // CHUNKED: per group, the source offsets (elements from the row start) and byte counts of its one or two pieces
   RQ256Piece* pieces = reinterpret_cast<RQ256Piece*>(stats + 64);
@@ -596,12 +597,21 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
 
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    if (lane == 0) warp_max[warp] = amax;
+    float* row_max = warp_max + (it & 1) * 32;
+    if (lane == 0) row_max[warp] = amax;
     if constexpr (ADALN) fence_proxy_async_smem();  // h in the row buffer, for the bulk stores below
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) record_error_rq(p.error_word);
       aborted = true;
       break;
+    }
+    if constexpr (!CHUNKED && !ADALN) {
+      // Plain rows: every thread has read its part of the row buffer (column phase), so it is refilled now; and the
+      // maxima of the next row go to the other set, so no second barrier is needed before the next row.
+      if (tid == 0) {
+        const int m_next = m + stages * gridDim.x;
+        if (m_next < p.M) issue_row(st, m_next);
+      }
     }
     if constexpr (ADALN) {
       if (tt == 0 && p.x_out) {  // each team stores its groups of h
@@ -612,7 +622,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
     float rmax = 0.0f;
-    for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, warp_max[w]);
+    for (int w = 0; w < nwarps; ++w) rmax = fmaxf(rmax, row_max[w]);
     float scale, inv;
     scale_and_inverse<ROUNDING>(__fmul_rn(rmax, kScale), scale, inv);
     const float inv_y = __fmul_rn(inv, kScale);
@@ -642,12 +652,13 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     }
     if (tid == 0) p.s[m] = scale;
     if constexpr (CHUNKED || ADALN) {
-      if (tt == 0 && p.x_out) bulk_wait_group_read<0>();  // the row stores have read this buffer
-    }
-    __syncthreads();
-    if (tid == 0) {
-      const int m_next = m + stages * gridDim.x;
-      if (m_next < p.M) issue_row(st, m_next);
+      // the row stores read this buffer until they are done, so it is refilled only after every thread saw them
+      if (tt == 0 && p.x_out) bulk_wait_group_read<0>();
+      __syncthreads();
+      if (tid == 0) {
+        const int m_next = m + stages * gridDim.x;
+        if (m_next < p.M) issue_row(st, m_next);
+      }
     }
   }
   if constexpr (CHUNKED || ADALN) {
