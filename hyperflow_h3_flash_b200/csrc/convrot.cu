@@ -395,10 +395,15 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
   if (two_sm) {
-    OutMaps ty;  // bf16 output, one map per chunk, 32 x 32 boxes for the epilogue's TMA stores
+    // bf16 output, one map per chunk: 32 x 64 boxes when every chunk (and so the whole output) is a multiple of 64
+    // columns wide, else 32 x 32
+    OutMaps ty;
     memset(&ty, 0, sizeof(ty));
+    p.wide_store = out_chunk % 64 == 0 ? 1 : 0;
+    const int box_cols = p.wide_store ? 64 : 32;
     for (int j = 0; j < n_chunks && !raw; ++j)
-      if ((rc = make_map(&ty.m[j], p.out_chunks[j], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, out_chunk, ldo, 32, 32)))
+      if ((rc = make_map(&ty.m[j], p.out_chunks[j], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, out_chunk, ldo, 32,
+                         box_cols)))
         return rc;
     if (raw) return launch_gemm2<Cfg2, EPI_RAW_I32, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);
     if (!has_lr) return launch_gemm2<Cfg2, EPI_DEQUANT, 0, 0>(*st, ta, tb, txa, tup, ty, p, stream);

@@ -58,6 +58,7 @@ struct GemmParams {
   int r;                // low-rank width (0 = none)
   int lr_seg_n;         // > 0: output columns [s lr_seg_n, (s + 1) lr_seg_n) read xa columns [s r, (s + 1) r)
   int split_k;          // > 1 (the bf16 down projection only): clusters of split_k CTAs split K, one tile each
+  int wide_store;       // 2-SM epilogue: 1 = stores leave as 32 x 64 boxes (128-byte rows), 0 = 32 x 32 boxes
   uint64_t wait_limit_ns;
   int* error_word;
 };
