@@ -600,14 +600,19 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     float* row_max = warp_max + (it & 1) * 32;
     if (lane == 0) row_max[warp] = amax;
     if constexpr (ADALN) fence_proxy_async_smem();  // h in the row buffer, for the bulk stores below
+    if constexpr (CHUNKED && !ADALN) {
+      // the gathered row's stores (issued when it landed) have read the buffer before the barrier below
+      if (tt == 0 && p.x_out) bulk_wait_group_read<0>();
+    }
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) record_error_rq(p.error_word);
       aborted = true;
       break;
     }
-    if constexpr (!CHUNKED && !ADALN) {
-      // Plain rows: every thread has read its part of the row buffer (column phase), so it is refilled now; and the
-      // maxima of the next row go to the other set, so no second barrier is needed before the next row.
+    if constexpr (!ADALN) {
+      // Every thread has read its part of the row buffer (column phase), and the gathered row's stores are done
+      // reading it, so it is refilled now; the maxima of the next row go to the other set, so no second barrier is
+      // needed before the next row.
       if (tid == 0) {
         const int m_next = m + stages * gridDim.x;
         if (m_next < p.M) issue_row(st, m_next);
@@ -651,7 +656,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
     if (tid == 0) p.s[m] = scale;
-    if constexpr (CHUNKED || ADALN) {
+    if constexpr (ADALN) {
       // the row stores read this buffer until they are done, so it is refilled only after every thread saw them
       if (tt == 0 && p.x_out) bulk_wait_group_read<0>();
       __syncthreads();
