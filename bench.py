@@ -515,6 +515,9 @@ def run_ours(args) -> None:
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e_ms = float(te.item())
+        barrier()
+        copies = copy_bound(torch, dev, x_host, y_host)  # all ranks at once, as in the e2e steps
+        barrier()
 
         # correctness of the whole step, exchange included: rows of this rank's output against the same layers run
         # on those rows alone on this GPU (no exchange; attention is identity, so out = to_out(to_v(x))).  1056
@@ -583,7 +586,9 @@ def run_ours(args) -> None:
             "config": workload_config(M, world, args.transport, args.peer_copies),
             "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2,
-                    "pipelining": "H2D / compute / D2H on three streams, double-buffered"},
+                    "pipelining": "H2D / compute / D2H on three streams, double-buffered",
+                    "copy_floor": copies,
+                    "frac_of_copy_floor": copies["floor_ms_per_step"] / (e2e_ms / args.steps)},
             "gpu_launches": launches,
             "roofline": roofline,
             "rotate_quant": {"bound": "hbm", "avg_launch_ms": rq_avg, "bytes_per_launch": rq_bytes,
@@ -733,6 +738,44 @@ def pipelined_e2e(torch, dev, step, x_host, y_host, args, barrier) -> float:
     torch.cuda.synchronize()
     barrier()
     return start.elapsed_time(end)
+
+
+def copy_bound(torch, dev, x_host, y_host, reps: int = 3) -> dict:
+    """The PCIe floor under the e2e number: the step's upload (x) and download (out) between the same pinned host
+    buffers and device memory, timed alone and both at once on two streams (best of `reps`, CUDA events)."""
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    xd = torch.empty_like(x_host, device=dev)
+    yd = torch.empty_like(y_host, device=dev)
+
+    def timed(fn) -> float:
+        best = None
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            best = s.elapsed_time(e) if best is None else min(best, s.elapsed_time(e))
+        return best
+
+    def both():
+        cur = torch.cuda.current_stream(dev)
+        up.wait_stream(cur)
+        down.wait_stream(cur)
+        with torch.cuda.stream(up):
+            xd.copy_(x_host, non_blocking=True)
+        with torch.cuda.stream(down):
+            y_host.copy_(yd, non_blocking=True)
+        cur.wait_stream(up)
+        cur.wait_stream(down)
+
+    h2d = timed(lambda: xd.copy_(x_host, non_blocking=True))
+    d2h = timed(lambda: y_host.copy_(yd, non_blocking=True))
+    duplex = timed(both)
+    nx, ny = x_host.numel() * x_host.element_size(), y_host.numel() * y_host.element_size()
+    return {"h2d_ms": h2d, "h2d_gbs": nx / (h2d * 1e-3) / 1e9, "d2h_ms": d2h, "d2h_gbs": ny / (d2h * 1e-3) / 1e9,
+            "both_at_once_ms": duplex, "floor_ms_per_step": max(h2d, d2h, duplex)}
 
 
 def reference_gpu_path(torch, I, dev, x, steps: int) -> dict:
