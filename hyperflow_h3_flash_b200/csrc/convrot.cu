@@ -591,7 +591,7 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   if (best_blocks < 1) best_blocks = 1;
   int best_stages = 1;
   for (int stages = 2; stages <= kRQMaxStages; ++stages) {
-    const size_t sm = rq256_smem_bytes(p.K, threads, stages, chunked);
+    const size_t sm = rq256_smem_bytes(p.K, threads, stages, chunked, adaln);
     if (sm > 227 * 1024 || static_cast<size_t>(best_blocks) * (sm + 1024) > 228 * 1024) break;
     best_stages = stages;
   }
@@ -599,7 +599,7 @@ int launch_rq256(const DeviceState& st, const RotQuantParams& p, cudaStream_t st
   q.stages = best_stages;
   if (g_rq_stages > 0) q.stages = g_rq_stages;
   if (g_rq_blocks > 0) best_blocks = g_rq_blocks;
-  const size_t smem = rq256_smem_bytes(p.K, threads, q.stages, chunked);
+  const size_t smem = rq256_smem_bytes(p.K, threads, q.stages, chunked, adaln);
   if (smem > 227 * 1024) return CONVROT_ERR_SHAPE;
   int64_t grid = static_cast<int64_t>(st.sms) * best_blocks;
   if (grid > p.M) grid = p.M;

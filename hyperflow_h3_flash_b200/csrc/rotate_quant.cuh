@@ -342,31 +342,35 @@ __global__ void __launch_bounds__(512) rotate_quant_kernel(const RotQuantParams 
 // ------------------------------------------------------------------------------------------------------------------
 // G = 256 kernel: a team of 8 threads per group, two columns per thread.
 //
-// The row lands in shared memory as one bulk copy per group, each into a 544-byte slot (512 + 32 bytes of pad), so
-// the four teams of a warp read disjoint banks.  Thread tt of a team loads the bf16 pair (columns 2tt, 2tt+1) of
-// every row a of the 16 x 16 group matrix (16 32-bit loads for 32 values), applies H16 along a to both columns, and
-// the team transposes through shared memory in two halves (rows 0-7, then 8-15; 128-bit stores and loads): thread
-// tt ends up with rows tt and tt+8, i.e. channels [16 tt, 16 tt + 16) and [16 (tt+8), ...) of the group, applies H16
-// along b, and writes 2 x 16 contiguous codes.
-constexpr int kSlotBytes = 544;
+// The row lands in shared memory as it lies in HBM: one bulk copy per row (per chunk of a chunked row), groups at
+// 512-byte strides.  Thread tt of a team loads the bf16 pair (columns 2tt, 2tt+1) of every row a of the 16 x 16 group
+// matrix (16 32-bit loads for 32 values), applies H16 along a to both columns, and the team transposes through shared
+// memory in two halves (rows 0-7, then 8-15; 128-bit stores and loads): thread tt ends up with rows tt and tt+8, i.e.
+// channels [16 tt, 16 tt + 16) and [16 (tt+8), ...) of the group, applies H16 along b, and writes 2 x 16 contiguous
+// codes.
+//
+// Bank order.  The four teams of a warp read four groups 512 bytes apart, i.e. the same banks for the same row a.
+// Team j (0..3 within its warp) therefore loads row a ^ j into register a.  H4' has the entry -1 exactly where
+// row ^ column == 3, so H4'[i ^ j][k] = H4'[i][k ^ j]: the column transform of the row-permuted input is the
+// transform's output permuted the same way (register k holds output row k ^ j), and the transpose stores register
+// 8h + a at row (8h + a) ^ j.  The operations are those of the unpermuted order up to commutation of the additions,
+// so the results are bitwise the same, and the four teams' loads hit four different rows' banks.
+constexpr int kSlotBytes = 512;        // one group of 256 bf16, unpadded (see "Bank order")
+constexpr int kPaddedSlotBytes = 544;  // the AdaLN form's slot: 32 bytes of pad put the warp's four groups on
+                                       // different banks without reordering the rows
 constexpr int kTrRow = 16 + kRQPadDoubles;  // doubles per transpose row
 
 // Threads of a chunked one-slot CTA at most (K <= 10240): bounding them lets the compiler keep that kernel within 96
 // registers, four CTAs per SM at K = 5120, like the plain kernel.
 constexpr int kRQ256ChunkedThreads = 320;
 
-struct RQ256Piece {
-  const __nv_bfloat16* src0;  // row 0's address of the group's first piece (add m * ldx for row m)
-  const __nv_bfloat16* src1;  // and of its second piece, when the group straddles two chunks
-  uint32_t bytes0, bytes1;    // bytes1 == 0: the group lies in one chunk
-};
-
-__host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages, bool chunked = false) {
-  const size_t slots = static_cast<size_t>(K / 256) * kSlotBytes;
+__host__ __device__ inline size_t rq256_smem_bytes(int K, int threads, int stages, bool chunked = false,
+                                                   bool adaln = false) {
+  const size_t slots = static_cast<size_t>(K / 256) * (adaln ? kPaddedSlotBytes : kSlotBytes);
   const size_t tr = static_cast<size_t>(threads / 8) * 8 * kTrRow * 8;  // per team: 8 rows of the half transpose
-  const size_t table = chunked ? static_cast<size_t>(K / 256) * sizeof(RQ256Piece) : 0;
+  (void)chunked;
   const size_t stats = 64 * 8;  // AdaLN: per-warp (sum, sum of squares) in fp64
-  return static_cast<size_t>(stages) * slots + tr + 64 * 4 + kRQMaxStages * 8 + stats + table + 64;
+  return static_cast<size_t>(stages) * slots + tr + 64 * 4 + kRQMaxStages * 8 + stats + 64;
 }
 
 // AdaLN on a pair of bf16 values (low half = even column): n = bf16((x - mean) * rstd) in fp32, then
@@ -396,8 +400,8 @@ __device__ __forceinline__ uint32_t adaln_pair(uint32_t w, uint32_t sc, uint32_t
 }
 
 // CHUNKED selects the chunked-row input (the Ulysses layouts, in this GPU's memory or gathered from the others'):
-// each row's copies come from a table of (address, bytes) pairs built once per CTA, so the per-row issue costs what
-// the plain walk costs, and x_out may receive each gathered row.  Plain rows (x_chunk == K) use the instantiation
+// one bulk copy per chunk of each row (K / x_chunk of them, 1280 bytes each for K = 5120 over 8 GPUs), and x_out may
+// receive each gathered row.  Plain rows (x_chunk == K) use the instantiation
 // without it.  The launch sizes residency from the compiled register count; at K = 5120 (160 threads) both forms
 // stay within 96 (plain 86 with no bound; chunked under its thread bound), so four CTAs fit an SM.
 template <int SLOTS, int ROUNDING, bool CHUNKED, bool ADALN = false>
@@ -408,63 +412,50 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
   const int ngroups = K / 256;
   const int nthr = blockDim.x;
   const int stages = p.stages;
-  const size_t stage_bytes = static_cast<size_t>(ngroups) * kSlotBytes;
+  constexpr int kSlot = ADALN ? kPaddedSlotBytes : kSlotBytes;
+  const size_t stage_bytes = static_cast<size_t>(ngroups) * kSlot;
   uint8_t* rows = rq2_smem_raw;
   double* tr = reinterpret_cast<double*>(rq2_smem_raw + stages * stage_bytes);
   // per-warp row maxima, two sets used by alternate rows (so plain rows need one block barrier per row)
   float* warp_max = reinterpret_cast<float*>(tr + static_cast<size_t>(nthr / 8) * 8 * kTrRow);
   uint64_t* bars = reinterpret_cast<uint64_t*>(warp_max + 64);
   double* stats = reinterpret_cast<double*>(bars + kRQMaxStages);  // ADALN: (sum, sum of squares) per warp
-  // CHUNKED: per group, the source offsets (elements from the row start) and byte counts of its one or two pieces
-  RQ256Piece* pieces = reinterpret_cast<RQ256Piece*>(stats + 64);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int nwarps = nthr >> 5;
   const int tt = tid & 7;                              // thread in team
+  // team in warp: the row order a ^ jx (see "Bank order").  The AdaLN form keeps the plain order in padded slots:
+  // its modulation operands, indexed by the row, would need per-row addresses, and the registers they take cost it a
+  // CTA per SM.
+  const int jx = ADALN ? 0 : (tid >> 3) & 3;
   const unsigned team_mask = 0xffu << (lane & ~7);     // the team's 8 lanes
   double* team_buf = tr + static_cast<size_t>(tid >> 3) * 8 * kTrRow;
   const uint32_t row_bytes = static_cast<uint32_t>(K) * 2;
   constexpr float kScale = 1.0f / 16.0f;  // 2^-L, L = 4
 
   auto issue_row = [&](int stage, int m) {
-    // one bulk copy per group into its padded slot (two when the group straddles a chunk of the input layout);
-    // all complete on the stage's barrier
+    // the row as it lies in HBM: one bulk copy (one per chunk of a chunked row), completing on the stage's barrier
     mbar_arrive_expect_tx(&bars[stage], row_bytes);
     const int64_t roff = static_cast<int64_t>(m) * p.ldx;
     uint8_t* dst = rows + stage * stage_bytes;
-    if constexpr (!CHUNKED) {
-      const __nv_bfloat16* src = p.x + roff;
-      for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlotBytes, src + g * 256, 512, &bars[stage]);
+    if constexpr (ADALN) {
+      for (int g = 0; g < ngroups; ++g) bulk_load(dst + g * kSlot, p.x + roff + g * 256, 512, &bars[stage]);
+    } else if constexpr (!CHUNKED) {
+      bulk_load(dst, p.x + roff, row_bytes, &bars[stage]);
     } else {
+      const uint32_t chunk_bytes = static_cast<uint32_t>(p.x_chunk) * 2;
+      const int nchunks = K / p.x_chunk;
 #pragma unroll 1
-      for (int g = 0; g < ngroups; ++g) {
-        const RQ256Piece pc = pieces[g];
-        bulk_load(dst + g * kSlotBytes, pc.src0 + roff, pc.bytes0, &bars[stage]);
-        if (pc.bytes1) bulk_load(dst + g * kSlotBytes + pc.bytes0, pc.src1 + roff, pc.bytes1, &bars[stage]);
-      }
+      for (int j = 0; j < nchunks; ++j) bulk_load(dst + j * chunk_bytes, select_chunk(p.xs, j) + roff, chunk_bytes,
+                                                  &bars[stage]);
     }
   };
 
   if (tid == 0) {
     for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
     fence_mbarrier_init();
-    if constexpr (CHUNKED) {
-      // x_chunk is a multiple of 128, so a group of 256 spans at most two chunks
-      for (int g = 0; g < ngroups; ++g) {
-        const int c0 = g * 256;
-        const int j = c0 / p.x_chunk;
-        const int c = c0 - j * p.x_chunk;
-        const int first = p.x_chunk - c < 256 ? p.x_chunk - c : 256;
-        RQ256Piece pc;
-        pc.src0 = select_chunk(p.xs, j) + c;
-        pc.src1 = first < 256 ? select_chunk(p.xs, j + 1) : nullptr;
-        pc.bytes0 = static_cast<uint32_t>(first) * 2;
-        pc.bytes1 = static_cast<uint32_t>(256 - first) * 2;
-        pieces[g] = pc;
-      }
-    }
   }
   __syncthreads();
   if (tid == 0)
@@ -482,11 +473,9 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     const bool arrived = mbar_wait_bounded(&bars[st], (it / stages) & 1, p.wait_limit_ns, &never);
     const uint8_t* xr = rows + st * stage_bytes;
     if constexpr (CHUNKED) {
-      // the gathered row, as it landed: the first thread of each group's team stores that group's slot
-      if (tt == 0 && p.x_out && arrived) {
-#pragma unroll 1
-        for (int g = tid >> 3; g < ngroups; g += nthr >> 3)
-          bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out + g * 256, xr + g * kSlotBytes, 512);
+      // the gathered row, as it landed, stored in one piece
+      if (tid == 0 && p.x_out && arrived) {
+        bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out, xr, row_bytes);
         bulk_commit_group();
       }
     }
@@ -505,7 +494,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       for (int sl = 0; sl < SLOTS; ++sl) {
         const int g = (tid + sl * nthr) >> 3;
         if (g >= ngroups) continue;
-        const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlotBytes) + tt;
+        const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlot) + tt;
 #pragma unroll
         for (int a = 0; a < 16; ++a) {
           const uint32_t w = col[a * 8];
@@ -547,15 +536,22 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
       // column phase: columns 2tt and 2tt+1 of the 16 x 16 group matrix
       double c0[16], c1[16];
-      const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlotBytes) + tt;
+      const uint32_t* col = reinterpret_cast<const uint32_t*>(xr + g * kSlot) + tt;
+      // a ^ jx = 4 (a >> 2) + ((a & 3) ^ jx): one base per a & 3, the rest an immediate offset
+      const uint32_t* colr[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) colr[r] = col + (r ^ jx) * 8;
 #pragma unroll
       for (int a = 0; a < 16; ++a) {
-        uint32_t w = col[a * 8];
+        // row a ^ jx, held in register a (the AdaLN form, in the plain order, addresses it directly: fewer registers)
+        uint32_t* src = ADALN ? const_cast<uint32_t*>(col) + a * 8 : const_cast<uint32_t*>(colr[a & 3]) + (a >> 2) * 32;
+        uint32_t w = *src;
         if constexpr (ADALN) {
-          // element (a, 2tt) of the group is column 256 g + 16 a + 2 tt of the row
-          w = adaln_pair(w, __ldg(scale_row + g * 128 + a * 8 + tt), __ldg(shift_row + g * 128 + a * 8 + tt), mean_f,
-                         rstd_f);
-          const_cast<uint32_t*>(col)[a * 8] = w;  // h replaces x in the row buffer (stored to x_out below)
+          // element (a ^ jx, 2tt) of the group is column 256 g + 16 (a ^ jx) + 2 tt of the row
+          const int ra = a ^ jx;
+          w = adaln_pair(w, __ldg(scale_row + g * 128 + ra * 8 + tt), __ldg(shift_row + g * 128 + ra * 8 + tt),
+                         mean_f, rstd_f);
+          *src = w;  // h replaces x in the row buffer (stored to x_out below)
         }
         c0[a] = static_cast<double>(__uint_as_float(w << 16));
         c1[a] = static_cast<double>(__uint_as_float(w & 0xffff0000u));
@@ -564,12 +560,15 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       h16_int(c1);
       // transpose in two halves: rows [8h, 8h + 8) go through the team buffer, thread tt takes row 8h + tt
       double v[2][16];
+      double* tbr[4];  // row (a ^ jx) of the half buffer = tbr[a & 3] + 4 (a >> 2) rows
+#pragma unroll
+      for (int r = 0; r < 4; ++r) tbr[r] = team_buf + (r ^ jx) * kTrRow + 2 * tt;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         __syncwarp(team_mask);
 #pragma unroll
-        for (int a = 0; a < 8; ++a)
-          *reinterpret_cast<double2*>(team_buf + a * kTrRow + 2 * tt) = make_double2(c0[8 * h + a], c1[8 * h + a]);
+        for (int a = 0; a < 8; ++a)  // register 8h + a holds row 8h + (a ^ jx)
+          *reinterpret_cast<double2*>(tbr[a & 3] + (a >> 2) * 4 * kTrRow) = make_double2(c0[8 * h + a], c1[8 * h + a]);
         __syncwarp(team_mask);
         const double2* rd = reinterpret_cast<const double2*>(team_buf + tt * kTrRow);
 #pragma unroll
@@ -601,8 +600,8 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     if (lane == 0) row_max[warp] = amax;
     if constexpr (ADALN) fence_proxy_async_smem();  // h in the row buffer, for the bulk stores below
     if constexpr (CHUNKED && !ADALN) {
-      // the gathered row's stores (issued when it landed) have read the buffer before the barrier below
-      if (tt == 0 && p.x_out) bulk_wait_group_read<0>();
+      // the gathered row's store (issued when it landed) has read the buffer before the barrier below
+      if (tid == 0 && p.x_out) bulk_wait_group_read<0>();
     }
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) record_error_rq(p.error_word);
@@ -619,10 +618,10 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
     if constexpr (ADALN) {
-      if (tt == 0 && p.x_out) {  // each team stores its groups of h
+      if (tt == 0 && p.x_out) {  // each team stores its groups of h (fenced by their writers before the barrier)
 #pragma unroll 1
         for (int g = tid >> 3; g < ngroups; g += nthr >> 3)
-          bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out + g * 256, xr + g * kSlotBytes, 512);
+          bulk_store(p.x_out + static_cast<int64_t>(m) * p.ld_out + g * 256, xr + g * kSlot, 512);
         bulk_commit_group();
       }
     }
@@ -657,7 +656,7 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
     }
     if (tid == 0) p.s[m] = scale;
     if constexpr (ADALN) {
-      // the row stores read this buffer until they are done, so it is refilled only after every thread saw them
+      // the stores of h read this buffer until they are done, so it is refilled only after every team saw them
       if (tt == 0 && p.x_out) bulk_wait_group_read<0>();
       __syncthreads();
       if (tid == 0) {
@@ -666,7 +665,10 @@ __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads :
       }
     }
   }
-  if constexpr (CHUNKED || ADALN) {
+  if constexpr (CHUNKED) {
+    if (tid == 0 && p.x_out) bulk_wait_group_all();
+  }
+  if constexpr (ADALN) {
     if (tt == 0 && p.x_out) bulk_wait_group_all();
   }
   if (aborted && tid == 0) {
