@@ -154,12 +154,17 @@ struct Gemm2Cfg {
   // lr_drain (epi_ready and lr_done per accumulator buffer and 128-column half)
   static constexpr int kNumBars = 2 * STAGES + 12 + 4;
   static constexpr int kBarBytes = ((kNumBars * 8 + 16 + 127) / 128) * 128;
-  // Output staging: per epilogue warp two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B) for TMA stores.
+  // Output staging per epilogue warp: two 32 x 32 bf16 boxes (2 KB each, SWIZZLE_64B), or in their place one
+  // 32 x 64 box (4 KB, SWIZZLE_128B) for wide stores; two wide boxes when shared memory has room for them, so that
+  // a box is written while the previous one's store (over NVLink, for a scattered output) still reads the other.
   static constexpr int kStoreBoxBytes = 32 * 64;
-  static constexpr int kStoreBytes = 4 * 2 * kStoreBoxBytes;
+  static constexpr int kWideBoxBytes = 32 * 128;
+  static constexpr int kSmemNoStore =
+      1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kBarBytes + kSiluTableBytes;
+  static constexpr int kWideBoxes = kSmemNoStore + 4 * 2 * kWideBoxBytes <= 227 * 1024 ? 2 : 1;
+  static constexpr int kStoreBytes = 4 * kWideBoxes * kWideBoxBytes;
   // After the barriers: the silu table of the SwiGLU epilogue (filled only by SwiGLU launches).
-  static constexpr int kSmemBytes =
-      1024 + STAGES * kStageBytes + kLRXaBytes + kLRUpBytes + kStoreBytes + kBarBytes + kSiluTableBytes;
+  static constexpr int kSmemBytes = kSmemNoStore + kStoreBytes;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory above the sm_100 per-CTA limit");
   static constexpr uint32_t kIdesc = make_idesc_i8(256, 256);
   static constexpr uint32_t kIdescLR = make_idesc_bf16(256, 128);  // one 128-column half per low-rank MMA
@@ -412,8 +417,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
     //    goes to the other GPU, 0.84 -> 0.70 ms);
     //  * otherwise two alternating 32 x 32 boxes (64-byte rows, SWIZZLE_64B: chunk c of row r at c ^ ((r >> 1) & 3)),
     //    one store per chunk.
-    uint8_t* my_boxes = store_stage + (warp - 2) * 2 * Cfg::kStoreBoxBytes;
-    int box_sel = 0;
+    uint8_t* my_boxes = store_stage + (warp - 2) * Cfg::kWideBoxes * Cfg::kWideBoxBytes;
+    int box_sel = 0;   // narrow boxes: which of the two 2 KB boxes
+    int wide_sel = 0;  // wide boxes: which of the kWideBoxes 4 KB boxes
     auto stage_and_store = [&](const float (&t)[32], int m_box, int n_col) {
       // A box wholly right of N has nothing to store; skipping it also keeps jy inside the maps that exist (with
       // one chunk of width N, n_col >= N would name chunk 1).  n_col is warp-uniform.
@@ -426,14 +432,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       }
       if (p.wide_store) {
         const bool first = (n_col & 63) == 0;  // the box's left half (the output width is a multiple of 64)
+        uint8_t* wbox = my_boxes + wide_sel * Cfg::kWideBoxBytes;
         if (first) {
-          if (lane == 0) bulk_wait_group_read<0>();  // the previous box's store has read the staging
+          // the store that last used this box has read it (with two boxes, the latest store may still be reading
+          // the other one)
+          if (lane == 0) bulk_wait_group_read<Cfg::kWideBoxes - 1>();
           __syncwarp();
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int pc = ((first ? 0 : 4) + c) ^ (lane & 7);
-          *reinterpret_cast<uint4*>(my_boxes + lane * 128 + pc * 16) =
+          *reinterpret_cast<uint4*>(wbox + lane * 128 + pc * 16) =
               make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
         }
         if (!first) {
@@ -442,9 +451,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
           if (lane == 0) {
             const int n_box = n_col - 32;
             const int jy = n_box / p.out_chunk;  // a 64-column box sits in one chunk (chunk widths % 64 == 0)
-            tma_store_2d(&tmap_y.m[jy], my_boxes, n_box - jy * p.out_chunk, m_box);
+            tma_store_2d(&tmap_y.m[jy], wbox, n_box - jy * p.out_chunk, m_box);
             bulk_commit_group();
           }
+          if constexpr (Cfg::kWideBoxes == 2) wide_sel ^= 1;
         }
         return;
       }
