@@ -1,4 +1,5 @@
-"""Exponent spans of 256-groups in the bench's synthetic activations (CPU).
+"""Facts about the rotation that the G = 256 kernel relies on (CPU): exponent spans of 256-groups in the bench's
+synthetic activations, and the exactness of the kernel's per-team row order.
 
 The rotation kernels sum each group in fp64 on integer-form values. That sum is exact while a group's nonzero
 magnitudes span at most 37 binades: floor(log2 max|x|) - floor(log2 min|x|) <= 37 for G = 256. This test pins that
@@ -43,3 +44,24 @@ def test_without_outlier_channels_few_groups_exceed_the_int32_width():
     s = spans(2048, 5120, 1.0)
     assert s.max() <= 37
     assert float((s > 14).mean()) < 0.05
+
+
+def test_row_order_a_xor_j_permutes_the_column_transform_exactly():
+    """The G = 256 kernel's team j loads row a ^ j of its 16 x 16 group matrix into register a (j = 0..3) so that
+    the four teams of a warp read different banks.  That is exact because H4' (the integer H4, -1 where
+    row ^ column == 3) satisfies H4'[i ^ j][k] = H4'[i][k ^ j]: the 16-point transform kron(H4', H4') of the
+    row-permuted input is the transform's output permuted the same way, for any input (checked here on random
+    integers, where every sum is exact)."""
+    from oracle import oracle as O
+
+    h16 = O.regular_hadamard(16) * 4  # kron(H4', H4') with integer entries
+    h4 = O.regular_hadamard(4) * 2
+    idx = np.arange(4)
+    for j in range(4):
+        assert np.array_equal(h4[idx ^ j], h4[:, idx ^ j])
+    rng = np.random.default_rng(3)
+    x = rng.integers(-(2**20), 2**20, size=(64, 16)).astype(np.float64)
+    a = np.arange(16)
+    for j in range(4):
+        permuted_in = x[:, a ^ j] @ h16  # register a holds row a ^ j
+        assert np.array_equal(permuted_in, (x @ h16)[:, a ^ j])  # register k holds output row k ^ j
