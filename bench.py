@@ -571,6 +571,11 @@ def run_ours(args) -> None:
     }
     if peak:
         roofline["cublaslt_int8_sustained_tops"] = peak["sustained_tops"]
+    bf16_sustained = measured_peak("bf16_tflops_sustained")
+    if bf16_sustained and achieved:
+        # the power-capped steady state: 2 x the seconds-long bf16 loop of MEASURED_PEAKS.json
+        roofline["peak_sustained"] = 2.0 * bf16_sustained
+        roofline["frac_of_sustained"] = achieved / (2.0 * bf16_sustained)
     rq_avg = statistics.mean(rq_ms) if rq_ms else None
     rq_bytes = M * K_DIM * 3 + 4 * M
     per_rank = [None] * world
