@@ -55,6 +55,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--peer-copies", default="",
                     help="peer transport: projections (of q, k, v) written locally and moved by the copy engines "
                          "while the next GEMM runs; the others store into the other GPUs' buffers from the epilogue")
+    ap.add_argument("--pull-chunks", type=int, default=0,
+                    help="peer transport: the copy engines pull the out projection's input in this many row chunks, "
+                         "each overlapping the previous chunk's out projection (0: the rotate kernel gathers it)")
     ap.add_argument("--case", choices=["gemm", "gemm_plain", "gemm_ffn_up", "rotate", "rotate_adaln", "rotate_ffn_down",
                                        "down", "step"],
                     default=None,
@@ -270,7 +273,7 @@ METRIC_DETAIL = ("value: INT8 TOPS of the config-2 linear set (the config-2 conv
 DATA = "synthetic (seeded, random-init weights)"
 
 
-def workload_config(rows: int, world: int, transport: str, peer_copies: str = "") -> dict:
+def workload_config(rows: int, world: int, transport: str, peer_copies: str = "", pull_chunks: int = 0) -> dict:
     """The `config` object of both arms' lines (the reference arm times a row sample of this same workload)."""
     exchange = world > 1 and transport == "peer"
     return {"workload": "config-2 linear set per rank: q,k,v (shared quantisation), out; "
@@ -278,8 +281,10 @@ def workload_config(rows: int, world: int, transport: str, peer_copies: str = ""
                         + (f"; Ulysses all-to-all of q,k,v [M/P,{HEADS},{HEAD_DIM}] around identity attention"
                            + ((" (over peer memory: " + (", ".join(peer_copies) + " written locally and moved by the "
                                                           "copy engines, " if peer_copies else "")
-                               + "the rest stored by the GEMM epilogue; gathered by the out projection's rotate "
-                                 "kernel)") if exchange else " (NCCL)")
+                               + "the rest stored by the GEMM epilogue; "
+                               + (f"pulled back by the copy engines in {pull_chunks} row chunks overlapping the out "
+                                  "projection)" if pull_chunks > 0 else "gathered by the out projection's rotate kernel)"))
+                              if exchange else " (NCCL)")
                            if world > 1 else ""),
             "rows_per_rank": rows, "total_rows": rows * world, "K": K_DIM, "N": N_DIM, "rank": RANK,
             "group": GROUP, "parallelism": f"ulysses{world}" if world > 1 else "single",
@@ -461,7 +466,8 @@ def run_ours(args) -> None:
     if world > 1 and args.transport == "peer":
         # every rank must agree on the transport: a rank whose mapping fails tells the others through an all-reduce
         try:
-            exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies))
+            exchange = ulysses.PeerExchange(M, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies),
+                                            pull_chunks=args.pull_chunks)
             failed = 0
         except Exception as e:  # noqa: BLE001 - reported, and the NCCL transport is used instead
             print(f"peer-memory exchange unavailable on rank {rank}: {e}; using NCCL all-to-all", file=sys.stderr)
@@ -594,7 +600,7 @@ def run_ours(args) -> None:
             "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": DATA,
-            "config": workload_config(M, world, args.transport, args.peer_copies),
+            "config": workload_config(M, world, args.transport, args.peer_copies, args.pull_chunks),
             "e2e": {"value": e2e_value, "unit": "TOPS", "ms_per_step": e2e_ms / args.steps,
                     "h2d_bytes_per_step": M * K_DIM * 2, "d2h_bytes_per_step": M * N_DIM * 2,
                     "pipelining": "H2D / compute / D2H on three streams, double-buffered",
@@ -662,7 +668,8 @@ def strong_scaling_cfg4(torch, dist, synthetic, ulysses, dev, rank, world, args,
     xs = synthetic.activations(rows, K_DIM, seed=100 + rank).to(dev)
     exchange = None
     if world > 1 and args.transport == "peer":
-        exchange = ulysses.PeerExchange(rows, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies))
+        exchange = ulysses.PeerExchange(rows, N_DIM, HEADS, device=dev, copy_names=tuple(args.peer_copies),
+                                        pull_chunks=args.pull_chunks)
 
     def step():
         return ulysses.attention_block_linears(xs, to_q, to_k, to_v, to_out, HEADS, exchange=exchange)

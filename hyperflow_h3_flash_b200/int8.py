@@ -243,18 +243,22 @@ class Int8RotLinear(nn.Module):
         kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
                                up=self.up.weight if self.rank else None, out_ptrs=out_ptrs, out_ld=out_ld)
 
-    def forward_gather(self, x_ptrs: list[int], rows: int, ldx: int, device: torch.device) -> Tensor:
+    def forward_gather(self, x_ptrs: list[int], rows: int, ldx: int, device: torch.device,
+                       out: Tensor | None = None) -> Tensor:
         """The layer on rows gathered from column chunks at device addresses (CUDA only): row m is the concatenation
         over j of row m of ``[rows, ldx]`` at ``x_ptrs[j]`` -- the head -> seq exchange done by the rotate kernel's
-        row copies, when the addresses are the other GPUs' buffers.  Returns ``[rows, out_features]``."""
+        row copies, when the addresses are the other GPUs' buffers.  Returns ``[rows, out_features]``, written into
+        ``out`` (bf16, contiguous rows) when given."""
         kernels = _kernels()
         Int8RotLinear._last_input.clear()
         self._lowrank_hit = None
         rounding = _lib.ROUND_KERNEL if rows >= _MIN_KERNEL_ROWS else _lib.ROUND_TORCH
         xq, sx, xg = kernels.rotate_quant_gather(x_ptrs, ldx, rows, self.in_features, self.group, device, rounding)
         xa = kernels.lowrank_down(xg, self.down.weight) if self.rank else None
-        return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa,
-                                      up=self.up.weight if self.rank else None)
+        up = self.up.weight if self.rank else None
+        if out is None:
+            return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa, up=up)
+        return kernels.convrot_matmul(xq, self.qweight, sx, self.wscale, bias=self.bias, xa=xa, up=up, out=out)
 
     def _forward_torch(self, x2: Tensor, rot: Tensor) -> Tensor:
         """The reference's torch path (int8.py:173-179): the rotation is rounded to bf16 and the codes divide by
@@ -469,7 +473,8 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
                    xa: Tensor | None = None, up: Tensor | None = None, out_chunks: int | None = None,
                    out_ptrs: list[int] | None = None, out_ld: int | None = None,
                    swiglu: bool = False, residual: Tensor | None = None, gate: Tensor | None = None,
-                   gate_index: Tensor | None = None, segments: int | None = None) -> Tensor | list[Tensor] | None:
+                   gate_index: Tensor | None = None, segments: int | None = None,
+                   out: Tensor | None = None) -> Tensor | list[Tensor] | None:
     """``bf16((acc * sa) * sb [+ bias] [+ xa . up^T])``, ``acc = a . b^T`` exact (int8.py:376-390 + extensions).
 
     ``out_chunks = P`` writes the result packed as ``[P, M, N / P]`` (the Ulysses send layout).  ``out_ptrs`` (device
@@ -481,7 +486,10 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
 
     ``segments = S`` treats b (and sb, bias, up) as S layers stacked along N that read the same input, and returns
     their S outputs ``[M, N / S]`` from one launch; ``xa`` is then ``[M, S * r]`` (layer s's down projection in columns
-    ``[s r, (s + 1) r)``) and ``up`` ``[N, r]``."""
+    ``[s r, (s + 1) r)``) and ``up`` ``[N, r]``.
+
+    ``out`` (plain form only: bf16 ``[M, N]``, unit column stride, rows 16-byte aligned) receives the result, which
+    is also returned."""
     _require(a, "a", torch.int8, 2)
     _require(b, "b", torch.int8, 2)
     M, K = a.shape
@@ -573,6 +581,16 @@ def convrot_matmul(a: Tensor, b: Tensor, sa: Tensor, sb: Tensor, *, bias: Tensor
                                             _stream(a))
         _lib.check(rc, "convrot_gemm_packed")
         return y
+    if out is not None:
+        if out.dtype != torch.bfloat16 or tuple(out.shape) != (M, N) or out.stride(1) != 1 or out.stride(0) % 8 \
+                or out.data_ptr() % 16 or out.device != a.device:
+            raise ValueError(f"out must be bf16 [{M}, {N}] on {a.device} with unit column stride and 16-byte rows")
+        rc = _lib.lib().convrot_gemm(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),
+                                     _ptr(bias), _ptr(xa), xa.stride(0) if xa is not None else 0, _ptr(up),
+                                     up.stride(0) if up is not None else 0, r, M, N, Kp, _ptr(out), out.stride(0),
+                                     _stream(a))
+        _lib.check(rc, "convrot_gemm")
+        return out
     ldy = -(-N // 8) * 8
     y = torch.empty(M, ldy, dtype=torch.bfloat16, device=a.device)
     rc = _lib.lib().convrot_gemm(_ptr(a_s), a_s.stride(0), _ptr(b_s), b_s.stride(0), _ptr(sa), _ptr(sb),

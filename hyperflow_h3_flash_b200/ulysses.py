@@ -98,7 +98,7 @@ class PeerExchange:
     _FLAG_BYTES = 4096
 
     def __init__(self, rows: int, width: int, heads: int, group=None, device: torch.device | None = None,
-                 copy_names: tuple[str, ...] = ()):
+                 copy_names: tuple[str, ...] = (), pull_chunks: int = 0):
         from . import _lib
 
         self._lib = _lib
@@ -109,6 +109,9 @@ class PeerExchange:
             raise ValueError(f"{heads} heads of width {width} cannot be exchanged over {self.P} ranks")
         self.rows, self.width, self.heads = rows, width, heads
         self.W = width // self.P
+        # pull_chunks = n > 0: the out projection's input is pulled by the copy engines in n row chunks into a local
+        # staging buffer, each chunk overlapping the previous chunk's out projection (see attention_block_peer)
+        self.pull_chunks = int(pull_chunks)
         self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self._tensor_bytes = self.P * rows * self.W * 2
         self.buf = torch.zeros(self._FLAG_BYTES + len(self._NAMES) * self._tensor_bytes, dtype=torch.uint8,
@@ -151,6 +154,8 @@ class PeerExchange:
             raise ValueError(f"copy_names must name q, k or v, got {copy_names!r}")
         self.copy_names = tuple(copy_names)
         self.copy_stream = torch.cuda.Stream(self.device)
+        self.pull_stage = (torch.empty(self.P, rows, self.W, dtype=torch.bfloat16, device=self.device)
+                           if self.pull_chunks > 0 else None)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=group)
 
@@ -183,6 +188,26 @@ class PeerExchange:
         stream = ctypes.c_void_p(self.copy_stream.cuda_stream)
         self._lib.check(self._lib.lib().convrot_copy_blocks(dst, src, nbytes, self.P, stream), "convrot_copy_blocks")
         packed.record_stream(self.copy_stream)  # not recycled by the allocator before the copies have read it
+
+    def pull_rows(self, name: str, r0: int, r1: int):
+        """Rows [r0, r1) of block ``rank`` of every other rank's buffer ``name`` (this rank's tokens, their heads)
+        into the staging buffer, by the copy engines on the copy stream, after the work queued so far on the current
+        stream.  Returns an event recorded after the copies and the P row addresses to read: the staging rows for
+        the other ranks, this rank's own buffer for itself."""
+        self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        row_bytes = self.W * 2
+        src_all = [b + r0 * row_bytes for b in self.block_ptrs(name)]
+        others = [j for j in range(self.P) if j != self.rank]
+        dst = (ctypes.c_void_p * len(others))(*[self.pull_stage[j, r0].data_ptr() for j in others])
+        src = (ctypes.c_void_p * len(others))(*[src_all[j] for j in others])
+        nbytes = (ctypes.c_size_t * len(others))(*([(r1 - r0) * row_bytes] * len(others)))
+        stream = ctypes.c_void_p(self.copy_stream.cuda_stream)
+        self._lib.check(self._lib.lib().convrot_copy_blocks(dst, src, nbytes, len(others), stream),
+                        "convrot_copy_blocks")
+        done = torch.cuda.Event()
+        done.record(self.copy_stream)
+        ptrs = [src_all[j] if j == self.rank else self.pull_stage[j, r0].data_ptr() for j in range(self.P)]
+        return done, ptrs
 
     def join_copies(self) -> None:
         torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
@@ -240,7 +265,21 @@ def attention_block_peer(x: Tensor, to_q, to_k, to_v, to_out, exchange: PeerExch
         source = "out"
     ex.signal(ex.READY)
     ex.wait(ex.READY)
-    return to_out.forward_gather(ex.block_ptrs(source), m, ex.W, x.device)
+    if ex.pull_chunks <= 0:
+        return to_out.forward_gather(ex.block_ptrs(source), m, ex.W, x.device)
+    # The copy engines pull chunk c's rows from the other ranks while the compute stream runs the out projection of
+    # chunk c - 1 on local memory (the chunk_block pattern, transformer.py:371-380); each chunk's output lands in
+    # its rows of y.  The compute stream waits for every pull before the step ends, so ARRIVED of the next step
+    # still follows this step's reads of the other ranks' buffers.
+    n = ex.pull_chunks
+    bounds = [(m * c // n, m * (c + 1) // n) for c in range(n)]
+    pulls = [ex.pull_rows(source, r0, r1) for r0, r1 in bounds]
+    y = torch.empty(m, to_out.out_features, dtype=torch.bfloat16, device=x.device)
+    compute = torch.cuda.current_stream(x.device)
+    for (r0, r1), (done, ptrs) in zip(bounds, pulls):
+        compute.wait_event(done)
+        to_out.forward_gather(ptrs, r1 - r0, ex.W, x.device, out=y[r0:r1])
+    return y
 
 
 def _packed_capable(x: Tensor, layers) -> bool:

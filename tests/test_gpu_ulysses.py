@@ -63,7 +63,7 @@ def _worker(rank, world, store_path, out_path):
         dist.destroy_process_group()
 
 
-def _worker_peer(rank, world, store_path, out_path, copy_names):
+def _worker_peer(rank, world, store_path, out_path, copy_names, pull_chunks=0):
     from hyperflow_h3_flash_b200 import int8 as I
     from hyperflow_h3_flash_b200 import synthetic, ulysses
 
@@ -74,7 +74,7 @@ def _worker_peer(rank, world, store_path, out_path, copy_names):
     ex = None
     try:
         to_q, to_k, to_v, to_out = _layers(dev)
-        ex = ulysses.PeerExchange(ROWS, K, HEADS, device=dev, copy_names=copy_names)
+        ex = ulysses.PeerExchange(ROWS, K, HEADS, device=dev, copy_names=copy_names, pull_chunks=pull_chunks)
         res = {}
         with torch.inference_mode():
             for step in range(3):  # the buffers and flags are reused step after step
@@ -97,13 +97,15 @@ def _worker_peer(rank, world, store_path, out_path, copy_names):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("copy_names", [("q", "k"), ()], ids=["copy_engines_qk", "epilogue_stores_only"])
-def test_peer_memory_exchange_on_two_gpus_equals_the_local_computation(tmp_path, copy_names):
+@pytest.mark.parametrize("copy_names,pull_chunks", [(("q", "k"), 0), ((), 0), ((), 3)],
+                         ids=["copy_engines_qk", "epilogue_stores_only", "out_projection_pulled_in_3_chunks"])
+def test_peer_memory_exchange_on_two_gpus_equals_the_local_computation(tmp_path, copy_names, pull_chunks):
     """The exchange over peer memory (GEMM stores into the other GPU, or local writes moved by the copy engines;
-    the rotate kernel reads from the other GPU) is bitwise the local computation, step after step."""
+    the rotate kernel reads from the other GPU, or the copy engines pull the out projection's input in row chunks)
+    is bitwise the local computation, step after step."""
     world = 2
-    mp.spawn(_worker_peer, args=(world, str(tmp_path / "store"), str(tmp_path / "out"), copy_names), nprocs=world,
-             join=True)
+    mp.spawn(_worker_peer, args=(world, str(tmp_path / "store"), str(tmp_path / "out"), copy_names, pull_chunks),
+             nprocs=world, join=True)
     for rank in range(world):
         res = torch.load(f"{tmp_path / 'out'}.{rank}")
         assert all(v is True for k, v in res.items() if k != "poll"), (rank, res)
