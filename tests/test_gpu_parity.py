@@ -803,3 +803,25 @@ def test_grouped_layers_follow_weight_updates():
         layers[0].up.weight.mul_(-1.0)
     outs = group(x)
     assert torch.equal(outs[0], layers[0](x)) and torch.equal(outs[1], layers[1](x))
+
+
+def test_convrot_matmul_into_a_row_slice_equals_the_plain_result():
+    """``out=`` (used by the chunked out projection) writes the plain result into rows of a larger buffer, bitwise,
+    leaving the other rows alone; a wrong dtype, shape or column stride is refused."""
+    M, K, N, r = 300, 1024, 512, 32
+    w = synthetic.linear_weights(K, N, rank=r, bias=True, group=256).to(DEV)
+    x = synthetic.activations(M, K, seed=71).to(DEV)
+    q, s = I.rotate_quant(x, 256)
+    xa = I.lowrank_down(x, w.down)
+    ref = I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up)
+    big = torch.full((M + 40, N), float("nan"), dtype=torch.bfloat16, device=DEV)
+    got = I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up, out=big[16:16 + M])
+    torch.cuda.synchronize()
+    assert got.data_ptr() == big[16].data_ptr()
+    assert torch.equal(big[16:16 + M], ref)
+    assert torch.isnan(big[:16].float()).all() and torch.isnan(big[16 + M:].float()).all()
+    for bad in (torch.empty(M, N - 8, dtype=torch.bfloat16, device=DEV),
+                torch.empty(M, N, dtype=torch.float32, device=DEV),
+                torch.empty(N, M, dtype=torch.bfloat16, device=DEV).t()):
+        with pytest.raises(ValueError, match="out must be"):
+            I.convrot_matmul(q, w.qweight, s, w.wscale, bias=w.bias, xa=xa, up=w.up, out=bad)
