@@ -179,4 +179,3 @@ def test_save_and_load_keep_storage_dtypes_and_outputs(tmp_path):
                       "down.weight": torch.bfloat16, "up.weight": torch.bfloat16}
     x = synthetic.activations(20, 256, seed=5)
     assert torch.equal(fresh(x), layer(x))
-
