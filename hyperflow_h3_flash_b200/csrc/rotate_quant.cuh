@@ -401,9 +401,9 @@ __device__ __forceinline__ uint32_t adaln_pair(uint32_t w, uint32_t sc, uint32_t
 
 // CHUNKED selects the chunked-row input (the Ulysses layouts, in this GPU's memory or gathered from the others'):
 // one bulk copy per chunk of each row (K / x_chunk of them, 1280 bytes each for K = 5120 over 8 GPUs), and x_out may
-// receive each gathered row.  Plain rows (x_chunk == K) use the instantiation
-// without it.  The launch sizes residency from the compiled register count; at K = 5120 (160 threads) both forms
-// stay within 96 (plain 86 with no bound; chunked under its thread bound), so four CTAs fit an SM.
+// receive each gathered row.  Plain rows (x_chunk == K) use the instantiation without it.  The launch sizes
+// residency from the compiled register count; at K = 5120 (160 threads) both forms stay within 96 (plain 92 with no
+// bound; chunked under its thread bound), so four CTAs fit an SM.
 template <int SLOTS, int ROUNDING, bool CHUNKED, bool ADALN = false>
 __global__ void __launch_bounds__(CHUNKED && SLOTS == 1 ? kRQ256ChunkedThreads : 512, CHUNKED && SLOTS == 1 ? 2 : 0)
     rotate_quant256_kernel(const RotQuantParams p) {
