@@ -59,6 +59,7 @@ struct GemmParams {
   int lr_seg_n;         // > 0: output columns [s lr_seg_n, (s + 1) lr_seg_n) read xa columns [s r, (s + 1) r)
   int split_k;          // > 1 (the bf16 down projection only): clusters of split_k CTAs split K, one tile each
   int wide_store;       // 2-SM epilogue: 1 = stores leave as 32 x 64 boxes (128-byte rows), 0 = 32 x 32 boxes
+  int group_m;          // tile order: M blocks per group (0: kGroupM)
   uint64_t wait_limit_ns;
   int* error_word;
 };
@@ -76,14 +77,16 @@ constexpr int kBM = 128;
 // Tile order of the persistent GEMMs: groups of kGroupM M blocks, and inside a group the M block varies fastest, then
 // the N block.  The tiles in flight at once (one per CTA or CTA pair) then cover a few M blocks times a few N blocks,
 // so the A rows and B rows they read stay in L2 even when B (the weights: 141 MB for a 5120 -> 27648 projection) is
-// larger than L2.  In plain row-major order every M block would stream all of B from HBM again.
+// larger than L2.  In plain row-major order every M block would stream all of B from HBM again.  kGroupM is the
+// default; a launch sets GemmParams::group_m (16 when B is larger than about 100 MB, so B streams half as often).
 constexpr int kGroupM = 8;
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-  const int group_tiles = kGroupM * num_n;
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb, int& nb) {
+  const int gm = group_m > 0 ? group_m : kGroupM;
+  const int group_tiles = gm * num_n;
   const int g = tile / group_tiles;
-  const int first = g * kGroupM;
-  const int rows = num_m - first < kGroupM ? num_m - first : kGroupM;
+  const int first = g * gm;
+  const int rows = num_m - first < gm ? num_m - first : gm;
   const int in = tile - g * group_tiles;
   mb = first + in % rows;
   nb = in / rows;
@@ -415,7 +418,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       bool ok = true;
       for (int tile = tile0; ok && tile < num_tiles; tile += tile_step) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
         const int m0 = mb * kBM;
         const int n0 = nb * BN;
         for (int kb = kb_begin; kb < kb_end; ++kb) {
@@ -507,7 +510,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       int i = 0;
       for (int tile = tile0; ok && tile < num_tiles; tile += tile_step, ++i) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
         const int m0 = mb * kBM;
         const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
         for (int h = 0; ok && h < 2; ++h) {
@@ -565,7 +568,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const uint32_t buf = i & 1;
       const uint32_t par = (i >> 1) & 1;
       int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
       const int m0 = mb * kBM;
       const int n0 = nb * BN;
       if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
@@ -706,7 +709,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     cluster_sync();
     if (warp >= 2 && warp <= 5 && tile0 < num_tiles) {
       int mb, nb;
-      tile_coords(tile0, num_m, num_n, mb, nb);
+      tile_coords(tile0, num_m, num_n, p.group_m, mb, nb);
       const int row_in_tile = (warp & 3) * 32 + lane;
       const int row = mb * kBM + row_in_tile;
       const int cols = BN / ksplit;  // a multiple of 4

@@ -271,7 +271,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       bool ok = true;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kBHalf;
         for (int kb = 0; kb < nkb; ++kb) {
@@ -353,7 +353,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       int i = 0;
       for (int tile = pair; ok && tile < num_tiles; tile += num_pairs, ++i) {
         int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
         const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         const int xs = p.lr_seg_n ? (nb * BN / p.lr_seg_n) * p.r : 0;  // this tile's segment of xa
         // Per half h, this CTA holds up rows [128 h + 64 rank, + 64) of the tile (the pair's N = 128 MMA splits its
@@ -481,7 +481,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::kThreads, 1)
       const uint32_t buf = i & 1;
       const uint32_t par = (i >> 1) & 1;
       int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      tile_coords(tile, num_m, num_n, p.group_m, mb, nb);
       const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
       const int n0 = nb * BN;
       if (!mbar_wait_bounded(&tmem_full[buf], par, limit, abort_flag)) {
