@@ -394,11 +394,12 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   p.lr_seg_n = lr_segments > 1 ? static_cast<int>(N / lr_segments) : 0;
   p.wait_limit_ns = g_wait_limit_ns;
   p.error_word = st->error_word;
-  // Weights larger than about 100 MB (config 3's FFN-up, 141.6 MB) do not stay in L2 between tile groups, so every
-  // group streams them from HBM again: 16 M blocks per group halve that (FFN-up with SwiGLU at M = 32768, 16 against
-  // 8 on one box: 3.08-3.12 against 3.16-3.18 ms); config 2's 26 MB weights keep the default 8 (0.556-0.565 ms
-  // either way).
-  p.group_m = static_cast<int64_t>(N) * K > (100LL << 20) ? 16 : 0;
+  // Weights above 64 MB do not stay in L2 between tile groups next to the streaming output, so every group reads
+  // them from HBM again: 16 M blocks per group halve that, while a group's A rows (16 x 256 x K bytes) stay at most
+  // 32 MB.  Measured at M = 32760-32768 on one box each, 16 against 8: FFN-up with SwiGLU (141.6 MB) 3.08-3.12
+  // against 3.16-3.18 ms, QKV (78.6 MB) 1.657-1.663 against 1.703-1.704 ms; FFN-down (70.8 MB, K = 13824: 57 MB of
+  // A per group) 1.496-1.498 against 1.475-1.480 ms, so it keeps 8; config 2 (26 MB) is the same either way.
+  p.group_m = static_cast<int64_t>(N) * K > (64LL << 20) && K <= 8192 ? 16 : 0;
   if (two_sm) {
     // bf16 output, one map per chunk: 32 x 64 boxes when every chunk (and so the whole output) is a multiple of 64
     // columns wide, else 32 x 32
