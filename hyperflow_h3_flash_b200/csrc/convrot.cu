@@ -398,8 +398,11 @@ int gemm_i8(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const fl
   // them from HBM again: 16 M blocks per group halve that, while a group's A rows (16 x 256 x K bytes) stay at most
   // 32 MB.  Measured at M = 32760-32768 on one box each, 16 against 8: FFN-up with SwiGLU (141.6 MB) 3.08-3.12
   // against 3.16-3.18 ms, QKV (78.6 MB) 1.657-1.663 against 1.703-1.704 ms; FFN-down (70.8 MB, K = 13824: 57 MB of
-  // A per group) 1.496-1.498 against 1.475-1.480 ms, so it keeps 8; config 2 (26 MB) is the same either way.
-  p.group_m = static_cast<int64_t>(N) * K > (64LL << 20) && K <= 8192 ? 16 : 0;
+  // A per group) 1.496-1.498 against 1.475-1.480 ms (and 1.61-1.62 ms with 4), so it keeps 8.  Weights of at most
+  // 32 MB stay in L2 anyway; there 4 M blocks per group measured 0.9 % faster than 8 (config 2, 26 MB, alternating
+  // runs on one box: 0.5695-0.5829 against 0.5760-0.5840 ms).
+  const int64_t b_bytes = static_cast<int64_t>(N) * K;
+  p.group_m = b_bytes <= (32LL << 20) ? 4 : b_bytes > (64LL << 20) && K <= 8192 ? 16 : 0;
   if (two_sm) {
     // bf16 output, one map per chunk: 32 x 64 boxes when every chunk (and so the whole output) is a multiple of 64
     // columns wide, else 32 x 32

@@ -78,7 +78,7 @@ constexpr int kBM = 128;
 // the N block.  The tiles in flight at once (one per CTA or CTA pair) then cover a few M blocks times a few N blocks,
 // so the A rows and B rows they read stay in L2 even when B (the weights: 141 MB for a 5120 -> 27648 projection) is
 // larger than L2.  In plain row-major order every M block would stream all of B from HBM again.  kGroupM is the
-// default; a launch sets GemmParams::group_m (16 when B is larger than about 100 MB, so B streams half as often).
+// default; a launch sets GemmParams::group_m by the size of B (4, 8 or 16 M blocks per group).
 constexpr int kGroupM = 8;
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb, int& nb) {
